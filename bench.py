@@ -1,0 +1,315 @@
+"""Benchmark of the trnsparse_b200 sparse compute path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (one JSON line on rank 0): config 2, CSR spmv ``y = 2.0 * A @ x`` on
+the 5-point Poisson Laplacian of a 2048x2048 grid (4,194,304 rows,
+20,963,328 nnz, int32 indices, fp32), reported as algorithmic HBM GB/s:
+bytes = 4*nnz (values) + 4*nnz (col idx) + 4*(n+1) (row ptr) + 4*n (x) + 4*n (y).
+Each timed step is one spmv launch on device-resident inputs; between steps
+a 512 MiB buffer is written so L2 (126 MB) holds nothing of the inputs, and
+only the kernel is inside the CUDA-event window. ``e2e`` times the public
+API call ``trnsparse_b200.spmv`` with the dense operand in pinned host
+memory: the host->device copy of x, the kernel and the device->host copy of
+y are inside the window.
+
+Secondary measurements (bsr_spmm TFLOP/s and the other configurations) are
+reported under ``extra``. With N > 1 (torchrun, one process per GPU, NCCL)
+every rank runs the headline workload on its own GPU (weak scaling, no
+data-path collective); time is the max over ranks.
+
+``--impl reference`` times the reference algorithm on the host CPU instead
+(the oracle restatement in ``oracle/``: ATen's CSR SpMV, all host threads),
+rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
+METRIC = BASELINE["metric"]
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, ws: int) -> float:
+    if ws == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class L2Flush:
+    def __init__(self, nbytes=512 << 20):
+        self.buf = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def timed_steps(step, steps: int, warmup: int, flush: L2Flush | None):
+    """Runs warmup + timed steps; returns per-step device milliseconds (kernel window only)."""
+    for _ in range(warmup):
+        if flush:
+            flush()
+        step()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        if flush:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+# --------------------------------------------------------------------------- workloads
+def spmv_bytes(A) -> int:
+    n = A.shape[0]
+    isz = A.row_ptrs.element_size()
+    return 4 * A.nnz + isz * A.nnz + isz * (n + 1) + 4 * n + 4 * n
+
+
+def run_ours(args, ws, rank, local):
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+
+    pk = peaks()
+    dev = torch.device("cuda", local)
+    A = w.poisson2d_csr(2048)
+    x_host = w.poisson_rhs(A.shape[0])
+    n = A.shape[0]
+    x = x_host.to(dev)
+    A.device_layout(dev)
+    nbytes = spmv_bytes(A)
+    flush = L2Flush()
+
+    def step():
+        return ts.spmv(A, x, alpha=2.0)
+
+    barrier(ws)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms = timed_steps(step, args.steps, args.warmup, flush)
+    total_ms = sum(ms)
+    total_ms = max_over_ranks(total_ms, ws)
+    ms_per_step = total_ms / args.steps
+    value = ws * nbytes / (ms_per_step * 1e-3) / 1e9
+
+    # e2e through the public API with host buffers
+    x_pin = x_host.pin_memory()
+
+    def e2e_step():
+        return ts.spmv(A, x_pin, alpha=2.0)
+
+    e2e_ms = timed_steps(e2e_step, args.steps, args.warmup, flush)
+    e2e_ms = max_over_ranks(sum(e2e_ms), ws) / args.steps
+    e2e_val = ws * nbytes / (e2e_ms * 1e-3) / 1e9
+
+    ach = nbytes / (statistics.median(ms) * 1e-3) / 1e9
+    line = {
+        "metric": METRIC,
+        "headline": "csr_spmv (config 2) algorithmic HBM GB/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded 5-point Poisson, x ~ N(0,1) seed 1)",
+        "config": {"workload": "config2_csr_spmv_poisson2048_alpha2", "rows": n, "nnz": A.nnz, "index": "int32",
+                   "bytes_per_step": nbytes, "l2": "flushed between steps (512 MiB write)",
+                   "parallelism": f"replica x{ws}"},
+        "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(ach / pk["hbm_gbs"], 4), "peak_source": pk["source"] + " (burst copy)",
+                     "traffic": None, "kernel": "csr_spmv_kernel<int,float>"},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_spmv(A, x_host)
+    return line
+
+
+def cpu_baseline_spmv(A, x_host, budget_s: float = 3.0) -> dict:
+    import oracle
+
+    nbytes = spmv_bytes(A)
+    oracle.csr_spmv(A.row_ptrs, A.col_indices, A.values, A.shape, x_host, 2.0)
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < budget_s or reps < 3:
+        oracle.csr_spmv(A.row_ptrs, A.col_indices, A.values, A.shape, x_host, 2.0)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"full config-2 spmv x{reps} (ATen CSR SpMV, as the reference's ops.py:30-48)",
+            "ms_per_call": round(dt * 1e3, 3)}
+
+
+def run_reference(args, ws, rank):
+    from trnsparse_b200 import workloads as w
+
+    if rank != 0:
+        return None
+    A = w.poisson2d_csr(2048)
+    x = w.poisson_rhs(A.shape[0])
+    import oracle
+
+    nbytes = spmv_bytes(A)
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        oracle.csr_spmv(A.row_ptrs, A.col_indices, A.values, A.shape, x, 2.0)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.csr_spmv(A.row_ptrs, A.col_indices, A.values, A.shape, x, 2.0)
+    dt = (time.perf_counter() - t0) / args.steps
+    val = nbytes / dt / 1e9
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(val, 3), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded 5-point Poisson)",
+        "config": {"workload": "config2_csr_spmv_poisson2048_alpha2", "rows": A.shape[0], "nnz": A.nnz,
+                   "index": "int32", "bytes_per_step": nbytes},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "full config-2 spmv per step (oracle restatement of ops.py:30-48, ATen CSR SpMV)"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, ws, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    ws, rank, local = dist_setup()
+    line = run_ours(args, ws, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

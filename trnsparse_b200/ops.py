@@ -1,0 +1,173 @@
+"""Sparse operations on B200 (reference API: trnsparse/ops.py).
+
+Every hot-path op keeps the reference's signature and semantics and runs on
+the GPU through the C ABI (``_lib.call``). Dense operands may live on the
+host or on the GPU: host inputs are copied to the current CUDA device and
+the result is copied back, so code written for the reference's CPU path gets
+the same (host) tensors back; CUDA inputs stay on the device. There is no CPU
+compute path and no backend switch.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .formats import BSRMatrix, COOMatrix, CSRMatrix
+
+
+def _dev_of(*ts: torch.Tensor | None) -> torch.device:
+    for t in ts:
+        if t is not None and t.is_cuda:
+            return t.device
+    return _lib.require_cuda()
+
+
+def _on(t: torch.Tensor | None, dev: torch.device, dtype: torch.dtype | None = None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    if t.device != dev or (dtype is not None and t.dtype != dtype):
+        t = t.to(device=dev, dtype=dtype, non_blocking=t.is_pinned() if t.device.type == "cpu" else False)
+    return t.contiguous()
+
+
+def _back(out: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """Return ``out`` on ``like``'s device; host results land in pinned memory."""
+    if like.is_cuda:
+        return out
+    host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    host.copy_(out, non_blocking=True)
+    torch.cuda.current_stream(out.device).synchronize()
+    return host
+
+
+# ---------------------------------------------------------------------------
+# CSR
+# ---------------------------------------------------------------------------
+
+
+def spmv(
+    A: CSRMatrix,
+    x: torch.Tensor,
+    alpha: float = 1.0,
+    y: torch.Tensor | None = None,
+    beta: float = 0.0,
+) -> torch.Tensor:
+    """``alpha * A @ x (+ beta * y)`` (reference: trnsparse/ops.py:30-48).
+
+    ``beta * y`` is added only when ``y is not None and beta != 0.0``. A 2-D
+    ``x`` is treated as a dense right-hand side (as ``sparse @ x`` would).
+    """
+    m, n = A.shape
+    assert x.shape[0] == n, f"Dimension mismatch: A is {A.shape}, x is {x.shape}"
+    if x.dim() == 2:
+        return spmm(A, x, alpha=alpha, C=y, beta=beta)
+    dev = _dev_of(x)
+    if x.dtype != A.dtype:
+        raise RuntimeError(f"spmv: dtype mismatch, A is {A.dtype} and x is {x.dtype}")
+    lay = A.device_layout(dev)
+    xd = _on(x, dev)
+    use_y = y is not None and beta != 0.0
+    yd = _on(y, dev, A.dtype) if use_y else None
+    if use_y:
+        yd = yd.expand(m).contiguous() if yd.dim() == 0 or yd.shape[0] != m else yd
+    out = torch.empty(m, dtype=A.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "trnsparse_csr_spmv", m, n, A.nnz, _lib.index_code(lay["row_ptrs"].dtype), _lib.dtype_code(A.dtype),
+            _lib.ptr(lay["row_ptrs"]), _lib.ptr(lay["col_indices"]), _lib.ptr(lay["values"]),
+            _lib.ptr(xd), float(alpha), _lib.ptr(yd), float(beta), _lib.ptr(out), _lib.stream_handle(dev),
+        )
+    return _back(out, x)
+
+
+def spmm(
+    A: CSRMatrix,
+    B: torch.Tensor,
+    alpha: float = 1.0,
+    C: torch.Tensor | None = None,
+    beta: float = 0.0,
+) -> torch.Tensor:
+    """``alpha * A @ B (+ beta * C)`` (reference: trnsparse/ops.py:51-78)."""
+    m, n = A.shape
+    assert B.shape[0] == n, f"Dimension mismatch: A is {A.shape}, B is {B.shape}"
+    if B.dim() == 1:
+        return spmv(A, B, alpha=alpha, y=C, beta=beta)
+    dev = _dev_of(B)
+    if B.dtype != A.dtype:
+        raise RuntimeError(f"spmm: dtype mismatch, A is {A.dtype} and B is {B.dtype}")
+    k = B.shape[1]
+    lay = A.device_layout(dev)
+    Bd = _on(B, dev)
+    use_c = C is not None and beta != 0.0
+    Cd = None
+    if use_c:
+        Cd = _on(C, dev, A.dtype)
+        if tuple(Cd.shape) != (m, k):
+            Cd = Cd.expand(m, k).contiguous()
+    out = torch.empty(m, k, dtype=A.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "trnsparse_csr_spmm", m, n, k, A.nnz, _lib.index_code(lay["row_ptrs"].dtype), _lib.dtype_code(A.dtype),
+            _lib.ptr(lay["row_ptrs"]), _lib.ptr(lay["col_indices"]), _lib.ptr(lay["values"]),
+            _lib.ptr(Bd), k, float(alpha), _lib.ptr(Cd), k, float(beta), _lib.ptr(out), k,
+            _lib.stream_handle(dev),
+        )
+    return _back(out, B)
+
+
+def spmv_symmetric(A: CSRMatrix, x: torch.Tensor, alpha: float = 1.0, uplo: str = "upper") -> torch.Tensor:
+    """``alpha * (A @ x + strict(A)^T @ x)`` for one stored triangle (ops.py:81-104).
+
+    Both products run through the CSR SpMV kernel; the transpose of the
+    strict triangle is built once on the host (structure only).
+    """
+    m, n = A.shape
+    assert m == n, "Matrix must be square for symmetric SpMV"
+    key = ("strict_T",) + tuple(A.row_ptrs.shape)
+    cached = A._dev.get(key)
+    if cached is None or cached[0] is not A.values:
+        coo = A.to_coo()
+        keep = coo.row_indices.cpu() != coo.col_indices.cpu()
+        strict_t = COOMatrix(
+            values=coo.values.cpu()[keep],
+            row_indices=coo.col_indices.cpu()[keep].to(torch.long),
+            col_indices=coo.row_indices.cpu()[keep].to(torch.long),
+            shape=(n, m),
+        ).to_csr()
+        cached = (A.values, strict_t)
+        A._dev[key] = cached
+    strict_t = cached[1]
+    return spmv(A, x, alpha=alpha) + spmv(strict_t, x, alpha=alpha)
+
+
+def sparse_add(A: CSRMatrix, B: CSRMatrix, alpha: float = 1.0, beta: float = 1.0) -> CSRMatrix:
+    """Pattern union ``alpha*A + beta*B`` (ops.py:107-133); structural host op."""
+    assert A.shape == B.shape, f"Shape mismatch: {A.shape} vs {B.shape}"
+    ca, cb = A.to_coo(), B.to_coo()
+    idx = torch.stack(
+        [torch.cat([ca.row_indices, cb.row_indices]), torch.cat([ca.col_indices.long(), cb.col_indices.long()])]
+    )
+    vals = torch.cat([alpha * ca.values, beta * cb.values])
+    csr = torch.sparse_coo_tensor(idx, vals, size=A.shape).coalesce().to_sparse_csr()
+    return CSRMatrix(values=csr.values(), col_indices=csr.col_indices(), row_ptrs=csr.crow_indices(), shape=A.shape)
+
+
+def sparse_scale(A: CSRMatrix, alpha: float) -> CSRMatrix:
+    """``alpha * A`` with copied structure (ops.py:136-143)."""
+    return CSRMatrix(
+        values=alpha * A.values, col_indices=A.col_indices.clone(), row_ptrs=A.row_ptrs.clone(), shape=A.shape
+    )
+
+
+def sparse_transpose(A: CSRMatrix) -> CSRMatrix:
+    """CSR of A^T (ops.py:146-154); structural host op."""
+    coo = A.to_coo()
+    return COOMatrix(
+        values=coo.values, row_indices=coo.col_indices, col_indices=coo.row_indices, shape=(A.shape[1], A.shape[0])
+    ).to_csr()
+
+
+def nnz_per_row(A: CSRMatrix) -> torch.Tensor:
+    """Stored entries per row (ops.py:157-159)."""
+    return A.row_ptrs[1:] - A.row_ptrs[:-1]
