@@ -72,6 +72,93 @@ TRNSPARSE_API int trnsparse_csr_spmm(int64_t m, int64_t n, int64_t k, int64_t nn
                        const void* B, int64_t ldb, double alpha, const void* C, int64_t ldc,
                        double beta, void* out, int64_t ldo, void* stream);
 
+
+/* Reads the device-side error word (first bounded wait that gave up, 0 if
+ * none) of the current device; clears it when `clear` is non-zero. Blocks
+ * until prior work on the device completes. */
+TRNSPARSE_API int trnsparse_device_error(int* code, int clear);
+
+/* ---- BSR geometry -------------------------------------------------------
+ * Every BSR entry point takes the same seven leading arguments, the device
+ * image of a reference BSRMatrix (trnsparse/formats.py:130-263):
+ *   m, n       element shape (padding to whole blocks is implicit)
+ *   b          block size
+ *   n_blocks   stored blocks
+ *   row_ptr    int32[ceil(m/b)+1]  block_row_ptrs
+ *   col_idx    int32[n_blocks]     block_col_indices
+ *   blocks     float[n_blocks*b*b] row-major blocks, contiguous
+ * b == 128 with m, n multiples of 128 takes the coalesced warp-per-row-slice
+ * kernels; other geometries take a generic thread-per-row kernel. */
+
+/* out = alpha * (A @ x) [+ beta * y]: the reference's bsr_spmm with one
+ * right-hand-side column (trnsparse/iterative.py:44-50 `_bsr_matvec`). */
+TRNSPARSE_API int trnsparse_bsr_spmv(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                       const int* col_idx, const float* blocks, const float* x, double alpha,
+                       const float* y, double beta, float* out, void* stream);
+
+/* ---- BSR conjugate gradient (trnsparse/iterative.py:53-145) --------------
+ * Device-resident PCG with the reference's control flow: zero right-hand
+ * side returns (x0, 0, 0.0); |p.Ap| < 1e-30 breaks (iters = max_iter);
+ * ||r||/||b|| < tol returns after that iteration. inv_d (nullable) is the
+ * Jacobi preconditioner 1/diag(A) (iterative.py:129-145).
+ * Workspace: trnsparse_bsr_cg_workspace_size(n, max_iter) bytes, 256-byte
+ * aligned; its first 64 bytes are the status record
+ *   { int32 done, iters, reason, pad; double rel; double bb; double pad[4]; }
+ * (reason: 1 converged, 2 max_iter, 3 breakdown, 4 zero rhs).
+ * Usage: cg_start once, then cg_iterate over consecutive ranges
+ * [k_begin, k_end) up to k_end = max_iter + 1 (the last range records the
+ * final status), polling `done` between ranges as often as wanted. x holds
+ * x0 on entry and is updated in place. */
+TRNSPARSE_API size_t trnsparse_bsr_cg_workspace_size(int64_t n, int max_iter);
+TRNSPARSE_API int trnsparse_bsr_cg_start(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                           const int* col_idx, const float* blocks, const float* b_vec, const float* x,
+                           int x_is_zero, const float* inv_d, int max_iter, void* ws, size_t ws_bytes,
+                           void* stream);
+TRNSPARSE_API int trnsparse_bsr_cg_iterate(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                             const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                             double tol, int max_iter, int k_begin, int k_end, void* ws, void* stream);
+
+/* Chebyshev semi-iteration, K fixed steps (trnsparse/iterative.py:193-253).
+ * alpha/beta: HOST arrays of K float32 coefficients (chebyshev_coeffs);
+ * x: x0 in, x_K out; work: 2n floats of device scratch; rr_out: device
+ * double receiving ||b - A x_K||^2. One fused SpMV launch per step. */
+TRNSPARSE_API int trnsparse_bsr_chebyshev(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                            const int* col_idx, const float* blocks, const float* b_vec,
+                            const float* alpha, const float* beta, int K, float* x, float* work,
+                            double* rr_out, void* stream);
+
+/* Richardson, x += omega (b - A x), K fixed steps (iterative.py:256-295);
+ * work: n floats of device scratch; rr_out as above. */
+TRNSPARSE_API int trnsparse_bsr_richardson(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                             const int* col_idx, const float* blocks, const float* b_vec, double omega,
+                             int K, float* x, float* work, double* rr_out, void* stream);
+
+/* acc = u . v accumulated in float64 (device scalar). */
+TRNSPARSE_API int trnsparse_dot(int64_t n, const float* u, const float* v, double* acc, void* stream);
+
+/* Power iteration (trnsparse/iterative.py:298-340). Same chunked protocol as
+ * CG: ranges [k_begin, k_end) up to max_iter + 1; k_begin == 0 starts from
+ * v0 (normalised on the device); the status record's `rel` field holds the
+ * eigenvalue; the final range (k_end == max_iter + 1) or
+ * trnsparse_bsr_power_finish writes the returned eigenvector into v. */
+TRNSPARSE_API size_t trnsparse_bsr_power_workspace_size(int64_t n, int max_iter);
+TRNSPARSE_API int trnsparse_bsr_power_iterate(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                const int* col_idx, const float* blocks, const float* v0, float* v,
+                                double tol, int max_iter, int k_begin, int k_end, void* ws,
+                                size_t ws_bytes, void* stream);
+TRNSPARSE_API int trnsparse_bsr_power_finish(int64_t n, float* v, int max_iter, void* ws, void* stream);
+
+/* ---- BSR x dense -------------------------------------------------------- */
+
+/* C = A @ B on CUDA cores (fp32 FMA), any block size: the reference's
+ * `_bsr_spmm_pytorch` (trnsparse/ops.py:162-192), which nki_bsr_spmm
+ * (trnsparse/nki/dispatch.py:372-381) accelerates. B is n x k with row
+ * stride ldb; C is m x k with row stride ldc (rows of empty block-rows are
+ * written as zeros). */
+TRNSPARSE_API int trnsparse_bsr_spmm_simt(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                            const int* col_idx, const float* blocks, const float* B, int64_t k,
+                            int64_t ldb, float* C, int64_t ldc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

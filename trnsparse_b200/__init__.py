@@ -11,7 +11,17 @@ __version__ = "0.6.0"
 
 from .backend import HAS_NKI, get_backend, set_backend
 from .formats import BSRMatrix, COOMatrix, CSRMatrix, eye_sparse, from_dense, from_scipy
+from .iterative import (
+    bsr_diagonal,
+    cg_bsr,
+    chebyshev_bsr,
+    chebyshev_coeffs,
+    jacobi_preconditioner_bsr,
+    power_iteration_bsr,
+    richardson_bsr,
+)
 from .ops import (
+    bsr_spmm,
     nnz_per_row,
     sparse_add,
     sparse_scale,
@@ -32,6 +42,7 @@ __all__ = [
     "spmv",
     "spmm",
     "spmv_symmetric",
+    "bsr_spmm",
     "sparse_add",
     "sparse_scale",
     "sparse_transpose",
@@ -40,6 +51,13 @@ __all__ = [
     "screen_quartets",
     "density_screen",
     "sparsity_stats",
+    "cg_bsr",
+    "chebyshev_bsr",
+    "chebyshev_coeffs",
+    "richardson_bsr",
+    "power_iteration_bsr",
+    "jacobi_preconditioner_bsr",
+    "bsr_diagonal",
     "HAS_NKI",
     "set_backend",
     "get_backend",

@@ -32,7 +32,27 @@ SIGNATURES: dict[str, list] = {
     "trnsparse_csr_spmv": [_i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _f64, _p, _f64, _p, _p],
     "trnsparse_csr_spmm": [_i64, _i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _i64, _f64, _p, _i64, _f64, _p, _i64, _p],
 }
-_RESTYPE = {"trnsparse_last_error": C.c_char_p}
+_BSR = [_i64, _i64, _i32, _i64, _p, _p, _p]  # m, n, b, n_blocks, row_ptr, col_idx, blocks
+_sz = C.c_size_t
+SIGNATURES.update({
+    "trnsparse_device_error": [C.POINTER(C.c_int), _i32],
+    "trnsparse_bsr_spmv": _BSR + [_p, _f64, _p, _f64, _p, _p],
+    "trnsparse_bsr_cg_workspace_size": [_i64, _i32],
+    "trnsparse_bsr_cg_start": _BSR + [_p, _p, _i32, _p, _i32, _p, _sz, _p],
+    "trnsparse_bsr_cg_iterate": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p],
+    "trnsparse_bsr_chebyshev": _BSR + [_p, _p, _p, _i32, _p, _p, _p, _p],
+    "trnsparse_bsr_richardson": _BSR + [_p, _f64, _i32, _p, _p, _p, _p],
+    "trnsparse_dot": [_i64, _p, _p, _p, _p],
+    "trnsparse_bsr_power_workspace_size": [_i64, _i32],
+    "trnsparse_bsr_power_iterate": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _sz, _p],
+    "trnsparse_bsr_power_finish": [_i64, _p, _i32, _p, _p],
+    "trnsparse_bsr_spmm_simt": _BSR + [_p, _i64, _i64, _p, _i64, _p],
+})
+_RESTYPE = {
+    "trnsparse_last_error": C.c_char_p,
+    "trnsparse_bsr_cg_workspace_size": C.c_size_t,
+    "trnsparse_bsr_power_workspace_size": C.c_size_t,
+}
 
 _lib = None
 
@@ -64,6 +84,18 @@ def load(path: Path | str | None = None) -> C.CDLL:
     if path is None:
         _lib = lib
     return lib
+
+
+def raw(name: str):
+    """The ctypes function object (for entry points that return a value, not a status)."""
+    return getattr(load(), name)
+
+
+def device_error(clear: bool = True) -> int:
+    """Device-side error word of the current device (0 = no bounded wait gave up)."""
+    v = C.c_int(0)
+    call("trnsparse_device_error", C.byref(v), 1 if clear else 0)
+    return v.value
 
 
 def call(name: str, *args) -> None:

@@ -34,6 +34,7 @@ NVCC_FLAGS = [
     "-Xcompiler",
     "-fvisibility=hidden",
     "--expt-relaxed-constexpr",
+    "-rdc=true",
     "-I",
     str(INCLUDE),
     "-I",

@@ -1,9 +1,12 @@
 // Error plumbing shared by every C-ABI entry point.
 #include "common.cuh"
+#include "ptx.cuh"
 
 #include <string.h>
 
 namespace tsb {
+
+__device__ int g_device_error = 0;
 
 static thread_local char g_last_error[512] = "";
 
@@ -37,3 +40,17 @@ int sm_count() {
 extern "C" const char* trnsparse_last_error(void) { return tsb::g_last_error; }
 
 extern "C" int trnsparse_version(void) { return 100; /* 0.1.0 */ }
+
+extern "C" int trnsparse_device_error(int* code, int clear) {
+  if (!code) return tsb::fail(TRNSPARSE_ERR_ARG, "device_error: null output");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, tsb::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return tsb::cuda_status(e, "device_error: read");
+  *code = v;
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(tsb::g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return tsb::cuda_status(e, "device_error: clear");
+  }
+  return TRNSPARSE_OK;
+}

@@ -14,6 +14,9 @@
 // (spmv: result = alpha * (A @ x); if y given and beta != 0: result + beta*y)
 // and ops.py:51-78 (spmm, same with a dense right-hand side).
 #include "common.cuh"
+#include "ptx.cuh"
+
+#include <stdlib.h>
 
 namespace tsb {
 namespace {
@@ -127,12 +130,26 @@ csr_spmv_kernel(int64_t m, int64_t nnz, const I* __restrict__ rp, const I* __res
   const Stage st = stage_rows<I, T>(smem, cap, rp, ci, v, nnz, r0, nrows, vec_ok, &rps, &vs, &cs);
 
   if (st.fits) {
-    const T* vrow = vs + st.dv;
+    // products v[j] * x[col[j]] element-parallel (every x gather of the slice
+    // is independent, so each thread keeps several in flight), in place
+    T* vrow = vs + st.dv;
     const I* crow = cs + st.dc;
+    const int span = static_cast<int>(st.e - st.s);
+    int q = threadIdx.x;
+    for (; q + 3 * kThreads < span; q += 4 * kThreads) {
+      const int64_t c0 = crow[q], c1 = crow[q + kThreads], c2 = crow[q + 2 * kThreads], c3 = crow[q + 3 * kThreads];
+      const T x0 = __ldg(x + c0), x1 = __ldg(x + c1), x2 = __ldg(x + c2), x3 = __ldg(x + c3);
+      vrow[q] = mul_rn(vrow[q], x0);
+      vrow[q + kThreads] = mul_rn(vrow[q + kThreads], x1);
+      vrow[q + 2 * kThreads] = mul_rn(vrow[q + 2 * kThreads], x2);
+      vrow[q + 3 * kThreads] = mul_rn(vrow[q + 3 * kThreads], x3);
+    }
+    for (; q < span; q += kThreads) vrow[q] = mul_rn(vrow[q], __ldg(x + static_cast<int64_t>(crow[q])));
+    __syncthreads();
     for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
       const int a = rps[r], b = rps[r + 1];
       T acc = T(0);
-      for (int j = a; j < b; ++j) acc += vrow[j] * __ldg(x + static_cast<int64_t>(crow[j]));
+      for (int j = a; j < b; ++j) acc = add_rn(acc, vrow[j]);
       out[r0 + r] = epilogue<T>(acc, alpha, y, beta, r0 + r);
     }
   } else {
@@ -144,6 +161,281 @@ csr_spmv_kernel(int64_t m, int64_t nnz, const I* __restrict__ rp, const I* __res
       for (int64_t j = a + lane; j < b; j += 32) acc += __ldg(v + j) * __ldg(x + static_cast<int64_t>(__ldg(ci + j)));
       acc = warp_sum(acc);
       if (lane == 0) out[r0 + r] = epilogue<T>(acc, alpha, y, beta, r0 + r);
+    }
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Pipelined SpMV: persistent CTAs, each walking its tiles (R rows each) with a
+// kStages-deep ring of shared-memory stages filled by 1-D bulk (TMA) copies
+// of the tile's row pointers, values and column indices, so several tiles'
+// loads stay in flight while earlier tiles are computed. Tiles whose slice
+// does not fit a stage (or the ragged last tile) are computed straight from
+// global memory.
+constexpr int kStages = 4;
+constexpr int kMaxTilesPerCta = 128;
+
+struct TileMeta {
+  int64_t s, e;  // nnz range of the tile
+  int dv, dc;    // offset of s inside the staged values / columns
+  int regular;
+  int pad;
+};
+
+template <typename I, typename T>
+struct PipeLayout {
+  int R, cap;
+  size_t rps_bytes, vals_bytes, cols_bytes, stage_bytes;
+  __host__ __device__ PipeLayout(int R_, int cap_) : R(R_), cap(cap_) {
+    rps_bytes = ((size_t)R * sizeof(I) + 15) & ~(size_t)15;
+    vals_bytes = ((size_t)(cap + 16) * sizeof(T) + 15) & ~(size_t)15;
+    cols_bytes = ((size_t)(cap + 16) * sizeof(I) + 15) & ~(size_t)15;
+    stage_bytes = rps_bytes + vals_bytes + cols_bytes;
+  }
+  static constexpr size_t head_bytes() {
+    return 64 /* barriers */ + kStages * sizeof(TileMeta) + 2 * kMaxTilesPerCta * sizeof(int64_t);
+  }
+  __host__ __device__ size_t total() const { return head_bytes() + kStages * stage_bytes + vals_bytes; }
+};
+
+template <typename I, typename T>
+__global__ void __launch_bounds__(kThreads)
+csr_spmv_pipe_kernel(int64_t m, int64_t nnz, const I* __restrict__ rp, const I* __restrict__ ci,
+                     const T* __restrict__ v, const T* __restrict__ x, T alpha, const T* __restrict__ y, T beta,
+                     T* __restrict__ out, int R, int cap, int64_t ntiles) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const PipeLayout<I, T> L(R, cap);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  TileMeta* meta = reinterpret_cast<TileMeta*>(smem + 64);
+  int64_t* bs = reinterpret_cast<int64_t*>(smem + 64 + kStages * sizeof(TileMeta));
+  int64_t* be = bs + kMaxTilesPerCta;
+  unsigned char* stages = smem + PipeLayout<I, T>::head_bytes();
+  T* prod = reinterpret_cast<T*>(stages + kStages * L.stage_bytes);
+  constexpr int VT = 16 / sizeof(T);
+  constexpr int VC = 16 / sizeof(I);
+
+  const int64_t G = gridDim.x;
+  const int nt = static_cast<int>((ntiles - blockIdx.x + G - 1) / G);
+  for (int i = threadIdx.x; i < nt; i += kThreads) {
+    const int64_t r0 = (blockIdx.x + i * G) * R;
+    bs[i] = static_cast<int64_t>(rp[r0]);
+    be[i] = static_cast<int64_t>(rp[r0 + R < m ? r0 + R : m]);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto stage_rps = [&](int s) { return reinterpret_cast<I*>(stages + s * L.stage_bytes); };
+  auto stage_vals = [&](int s) { return reinterpret_cast<T*>(stages + s * L.stage_bytes + L.rps_bytes); };
+  auto stage_cols = [&](int s) {
+    return reinterpret_cast<I*>(stages + s * L.stage_bytes + L.rps_bytes + L.vals_bytes);
+  };
+
+  // thread 0: start loading tile i into stage i % kStages
+  auto fill = [&](int i) {
+    const int s = i % kStages;
+    const int64_t r0 = (blockIdx.x + i * G) * R;
+    const int64_t S = bs[i], E = be[i];
+    const int64_t s0v = S & ~(int64_t)(VT - 1), e1v = (E + VT - 1) & ~(int64_t)(VT - 1);
+    const int64_t s0c = S & ~(int64_t)(VC - 1), e1c = (E + VC - 1) & ~(int64_t)(VC - 1);
+    TileMeta mt;
+    mt.s = S;
+    mt.e = E;
+    mt.dv = static_cast<int>(S - s0v);
+    mt.dc = static_cast<int>(S - s0c);
+    mt.regular = (r0 + R <= m) && (E > S) && (E - S <= cap) && (e1v <= nnz) && (e1c <= nnz);
+    mt.pad = 0;
+    meta[s] = mt;
+    if (mt.regular) {
+      const uint32_t bv = static_cast<uint32_t>((e1v - s0v) * sizeof(T));
+      const uint32_t bc = static_cast<uint32_t>((e1c - s0c) * sizeof(I));
+      const uint32_t br = static_cast<uint32_t>(R * sizeof(I));
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bars[s], br + bv + bc);
+      bulk_g2s(stage_rps(s), rp + r0, br, &bars[s]);
+      bulk_g2s(stage_vals(s), v + s0v, bv, &bars[s]);
+      bulk_g2s(stage_cols(s), ci + s0c, bc, &bars[s]);
+    } else {
+      mbar_arrive(&bars[s]);
+    }
+  };
+
+  if (threadIdx.x == 0)
+    for (int i = 0; i < nt && i < kStages; ++i) fill(i);
+
+  for (int i = 0; i < nt; ++i) {
+    const int s = i % kStages;
+    if (!mbar_wait(&bars[s], (i / kStages) & 1)) return;
+    const TileMeta mt = meta[s];
+    const int64_t r0 = (blockIdx.x + i * G) * R;
+    if (mt.regular) {
+      const T* vals = stage_vals(s) + mt.dv;
+      const I* cols = stage_cols(s) + mt.dc;
+      const int span = static_cast<int>(mt.e - mt.s);
+      int q = threadIdx.x;
+      for (; q + 3 * kThreads < span; q += 4 * kThreads) {
+        const int64_t c0 = cols[q], c1 = cols[q + kThreads], c2 = cols[q + 2 * kThreads], c3 = cols[q + 3 * kThreads];
+        const T x0 = __ldg(x + c0), x1 = __ldg(x + c1), x2 = __ldg(x + c2), x3 = __ldg(x + c3);
+        prod[q] = mul_rn(vals[q], x0);
+        prod[q + kThreads] = mul_rn(vals[q + kThreads], x1);
+        prod[q + 2 * kThreads] = mul_rn(vals[q + 2 * kThreads], x2);
+        prod[q + 3 * kThreads] = mul_rn(vals[q + 3 * kThreads], x3);
+      }
+      for (; q < span; q += kThreads) prod[q] = mul_rn(vals[q], __ldg(x + static_cast<int64_t>(cols[q])));
+      __syncthreads();
+      const I* rps = stage_rps(s);
+      for (int r = threadIdx.x; r < R; r += kThreads) {
+        const int a = static_cast<int>(static_cast<int64_t>(rps[r]) - mt.s);
+        const int b = static_cast<int>((r + 1 < R ? static_cast<int64_t>(rps[r + 1]) : mt.e) - mt.s);
+        T acc = T(0);
+        for (int j = a; j < b; ++j) acc = add_rn(acc, prod[j]);
+        out[r0 + r] = epilogue<T>(acc, alpha, y, beta, r0 + r);
+      }
+    } else {
+      const int nrows = static_cast<int>(m - r0 < R ? m - r0 : R);
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+      for (int r = warp; r < nrows; r += kThreads / 32) {
+        const int64_t a = static_cast<int64_t>(rp[r0 + r]), b = static_cast<int64_t>(rp[r0 + r + 1]);
+        T acc = T(0);
+        for (int64_t j = a + lane; j < b; j += 32) acc += __ldg(v + j) * __ldg(x + static_cast<int64_t>(__ldg(ci + j)));
+        acc = warp_sum(acc);
+        if (lane == 0) out[r0 + r] = epilogue<T>(acc, alpha, y, beta, r0 + r);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kStages < nt) fill(i + kStages);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Warp-chunk SpMV: each warp owns chunks of 32*RW consecutive rows. Lane l
+// reads row_ptrs[r0 + l + 32 t] (coalesced loads), the warp loads the chunk's
+// slice of values / column indices with 16-byte vector loads, every lane
+// gathers x for its vector chunks (independent loads, all in flight
+// together), products go to a warp-private shared-memory strip and lane l
+// sums rows r0 + l + 32 t from it. There is no CTA-wide barrier: the 8 warps
+// of a CTA run independent chains, and the next chunk's row pointers are
+// prefetched before the current chunk is computed. A chunk whose slice
+// exceeds the strip is done row by row by the whole warp.
+template <typename I, typename T, int RW, int STRIP>
+__global__ void __launch_bounds__(kThreads)
+csr_spmv_warp_kernel(int64_t m, int64_t nnz, const I* __restrict__ rp, const I* __restrict__ ci,
+                     const T* __restrict__ v, const T* __restrict__ x, T alpha, const T* __restrict__ y, T beta,
+                     T* __restrict__ out) {
+  constexpr int VT = 16 / sizeof(T);
+  constexpr int ROWS = 32 * RW;
+  __shared__ __align__(16) T strip_all[kThreads / 32][STRIP + 8];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  T* strip = strip_all[w];
+  const int64_t nchunks = (m + ROWS - 1) / ROWS;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  int64_t chunk = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + w;
+  // lane l holds rp[r0 + l + 32 t] in pa[t]; pe = rp[r0 + ROWS] (clamped to m)
+  int64_t pa[RW], pe = 0;
+  auto load_ptrs = [&](int64_t c) {
+    const int64_t r0 = c * ROWS;
+#pragma unroll
+    for (int t = 0; t < RW; ++t) pa[t] = static_cast<int64_t>(__ldg(rp + min(r0 + lane + 32 * t, m)));
+    pe = static_cast<int64_t>(__ldg(rp + min(r0 + ROWS, m)));
+  };
+  if (chunk < nchunks) load_ptrs(chunk);
+  for (; chunk < nchunks; chunk += stride) {
+    const int64_t r0 = chunk * ROWS;
+    int64_t a[RW], b[RW];
+#pragma unroll
+    for (int t = 0; t < RW; ++t) a[t] = pa[t];
+#pragma unroll
+    for (int t = 0; t < RW; ++t) {
+      b[t] = __shfl_down_sync(0xffffffffu, a[t], 1);
+      const int64_t nextfirst = (t + 1 < RW) ? __shfl_sync(0xffffffffu, a[t + 1 < RW ? t + 1 : t], 0) : pe;
+      if (lane == 31) b[t] = nextfirst;
+    }
+    const int64_t s = __shfl_sync(0xffffffffu, a[0], 0);
+    const int64_t e = pe;
+    const int64_t nxt = chunk + stride;
+    if (nxt < nchunks) load_ptrs(nxt);
+    const int64_t s0 = s & ~(int64_t)(VT - 1);
+    if (e - s0 <= STRIP) {
+      const int nv = static_cast<int>((e - s0 + VT - 1) / VT);
+      constexpr int kPer = (STRIP / VT + 31) / 32;
+      T vv[kPer][VT];
+      I cc[kPer][VT];
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) {
+        const int c = lane + 32 * t;
+        const int64_t g = s0 + static_cast<int64_t>(c) * VT;
+        if (c < nv) {
+          if (g + VT <= nnz) {
+            typename Vec16<T>::type q = __ldcs(reinterpret_cast<const typename Vec16<T>::type*>(v + g));
+            const T* qp = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int u = 0; u < VT; ++u) vv[t][u] = qp[u];
+            if constexpr (sizeof(I) * VT == 16) {
+              int4 ic = __ldcs(reinterpret_cast<const int4*>(ci + g));
+              const I* ip = reinterpret_cast<const I*>(&ic);
+#pragma unroll
+              for (int u = 0; u < VT; ++u) cc[t][u] = ip[u];
+            } else {
+#pragma unroll
+              for (int u = 0; u < VT; ++u) cc[t][u] = ci[g + u];
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < VT; ++u) {
+              vv[t][u] = (g + u < nnz) ? v[g + u] : T(0);
+              cc[t][u] = (g + u < nnz) ? ci[g + u] : I(0);
+            }
+          }
+        }
+      }
+      T xv[kPer][VT];
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) {
+        const int c = lane + 32 * t;
+        const int64_t g = s0 + static_cast<int64_t>(c) * VT;
+#pragma unroll
+        for (int u = 0; u < VT; ++u)
+          xv[t][u] = (c < nv && g + u >= s && g + u < e) ? __ldg(x + static_cast<int64_t>(cc[t][u])) : T(0);
+      }
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) {
+        const int c = lane + 32 * t;
+        if (c < nv) {
+#pragma unroll
+          for (int u = 0; u < VT; ++u) strip[c * VT + u] = mul_rn(vv[t][u], xv[t][u]);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int t = 0; t < RW; ++t) {
+        const int64_t row = r0 + lane + 32 * t;
+        if (row < m) {
+          T acc = T(0);
+          const int lo = static_cast<int>(a[t] - s0), hi = static_cast<int>(b[t] - s0);
+          for (int j = lo; j < hi; ++j) acc = add_rn(acc, strip[j]);
+          out[row] = epilogue<T>(acc, alpha, y, beta, row);
+        }
+      }
+      __syncwarp();
+    } else {
+      const int nrows = static_cast<int>(m - r0 < ROWS ? m - r0 : ROWS);
+      for (int r = 0; r < nrows; ++r) {
+        int64_t ra = 0, rb = 0;
+#pragma unroll
+        for (int t = 0; t < RW; ++t) {
+          const int64_t ta = __shfl_sync(0xffffffffu, a[t], r & 31);
+          const int64_t tb = __shfl_sync(0xffffffffu, b[t], r & 31);
+          if ((r >> 5) == t) { ra = ta; rb = tb; }
+        }
+        T acc = T(0);
+        for (int64_t j = ra + lane; j < rb; j += 32) acc += __ldg(v + j) * __ldg(x + static_cast<int64_t>(__ldg(ci + j)));
+        acc = warp_sum(acc);
+        if (lane == 0) out[r0 + r] = epilogue<T>(acc, alpha, y, beta, r0 + r);
+      }
     }
   }
 }
@@ -208,6 +500,11 @@ csr_spmm_kernel(int64_t m, int64_t k, int64_t nnz, const I* __restrict__ rp, con
   }
 }
 
+inline int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
+
 // Rows per CTA so that a CTA stages about `target` stored entries.
 inline int pick_rows(int64_t m, int64_t nnz, int target) {
   double avg = m > 0 ? static_cast<double>(nnz) / static_cast<double>(m) : 1.0;
@@ -227,11 +524,50 @@ size_t smem_bytes(int rows, int cap) {
 template <typename I, typename T>
 int launch_spmv(int64_t m, int64_t nnz, const void* rp, const void* ci, const void* v, const void* x,
                 double alpha, const void* y, double beta, void* out, cudaStream_t st) {
-  const int rows = pick_rows(m, nnz, 4096);
+  static const int target = env_int("TRNSPARSE_SPMV_TILE", 640);  // tile holds target..2*target entries
+  const bool vec_ok = aligned16(v) && aligned16(ci) && aligned16(rp);
   const double avg = m > 0 ? static_cast<double>(nnz) / m : 0.0;
+  static const int variant = env_int("TRNSPARSE_SPMV_VARIANT", 2);  // 0 staged, 1 pipelined, 2 warp-chunk
+  if (vec_ok && variant >= 2) {
+    auto kern = variant == 2 ? csr_spmv_warp_kernel<I, T, 2, 384> : csr_spmv_warp_kernel<I, T, 1, 192>;
+    constexpr int kRowsPer = 64;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
+    if (e != cudaSuccess) return cuda_status(e, "csr_spmv: occupancy");
+    const int64_t nchunks = (m + (variant == 2 ? kRowsPer : 32) - 1) / (variant == 2 ? kRowsPer : 32);
+    int64_t grid = static_cast<int64_t>(sm_count()) * (per_sm < 1 ? 1 : per_sm);
+    const int64_t need = (nchunks + kThreads / 32 - 1) / (kThreads / 32);
+    if (grid > need) grid = need;
+    kern<<<(unsigned)grid, kThreads, 0, st>>>(m, nnz, (const I*)rp, (const I*)ci, (const T*)v, (const T*)x,
+                                              (T)alpha, (const T*)y, (T)beta, (T*)out);
+    TSB_CHECK_LAUNCH("csr_spmv launch");
+    return TRNSPARSE_OK;
+  }
+  if (vec_ok && variant == 1) {
+    int R = pick_rows(m, nnz, 2 * target);  // pick_rows halves: ~target entries per tile
+    int cap = static_cast<int>(R * avg * 1.25) + 64;
+    const PipeLayout<I, T> L(R, cap);
+    const size_t sm = L.total();
+    auto kern = csr_spmv_pipe_kernel<I, T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return cuda_status(e, "csr_spmv: set smem");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, sm);
+    if (e != cudaSuccess) return cuda_status(e, "csr_spmv: occupancy");
+    if (per_sm < 1) per_sm = 1;
+    const int64_t ntiles = (m + R - 1) / R;
+    int64_t grid = static_cast<int64_t>(sm_count()) * per_sm;
+    if (grid > ntiles) grid = ntiles;
+    if (grid * kMaxTilesPerCta < ntiles) grid = (ntiles + kMaxTilesPerCta - 1) / kMaxTilesPerCta;
+    if (grid > 0x7fffffff) return fail(TRNSPARSE_ERR_ARG, "csr_spmv: m=%lld too large", (long long)m);
+    kern<<<(unsigned)grid, kThreads, sm, st>>>(m, nnz, (const I*)rp, (const I*)ci, (const T*)v, (const T*)x,
+                                               (T)alpha, (const T*)y, (T)beta, (T*)out, R, cap, ntiles);
+    TSB_CHECK_LAUNCH("csr_spmv launch");
+    return TRNSPARSE_OK;
+  }
+  const int rows = pick_rows(m, nnz, 4096);
   int cap = static_cast<int>(rows * avg * 1.25) + 256;
   if (cap > 8192) cap = 8192;
-  const bool vec_ok = aligned16(v) && aligned16(ci);
   const size_t sm = smem_bytes<I, T>(rows, cap);
   auto kern = csr_spmv_kernel<I, T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
@@ -239,7 +575,7 @@ int launch_spmv(int64_t m, int64_t nnz, const void* rp, const void* ci, const vo
   const int64_t grid = (m + rows - 1) / rows;
   if (grid > 0x7fffffff) return fail(TRNSPARSE_ERR_ARG, "csr_spmv: m=%lld too large", (long long)m);
   kern<<<(unsigned)grid, kThreads, sm, st>>>(m, nnz, (const I*)rp, (const I*)ci, (const T*)v, (const T*)x,
-                                             (T)alpha, (const T*)y, (T)beta, (T*)out, rows, cap, vec_ok);
+                                             (T)alpha, (const T*)y, (T)beta, (T*)out, rows, cap, aligned16(v) && aligned16(ci));
   TSB_CHECK_LAUNCH("csr_spmv launch");
   return TRNSPARSE_OK;
 }

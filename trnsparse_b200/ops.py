@@ -171,3 +171,48 @@ def sparse_transpose(A: CSRMatrix) -> CSRMatrix:
 def nnz_per_row(A: CSRMatrix) -> torch.Tensor:
     """Stored entries per row (ops.py:157-159)."""
     return A.row_ptrs[1:] - A.row_ptrs[:-1]
+
+
+# ---------------------------------------------------------------------------
+# BSR
+# ---------------------------------------------------------------------------
+
+
+def _bsr_geometry(A: BSRMatrix, dev: torch.device, dtype: torch.dtype = torch.float32) -> tuple:
+    """The seven leading BSR arguments of the C ABI for ``A`` on ``dev``."""
+    lay = A.device_layout(dev)
+    blocks = lay["blocks"]
+    if blocks.dtype != dtype:
+        key = ("blocks", dtype)
+        if lay.get(key) is None:
+            lay[key] = blocks.to(dtype).contiguous()
+        blocks = lay[key]
+    m, n = A.shape
+    return (m, n, A.block_size, A.n_blocks, lay["row_ptr"].data_ptr(), lay["col_idx"].data_ptr(), blocks.data_ptr())
+
+
+def bsr_spmm(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
+    """``C = A @ B`` for a BSR ``A`` and dense ``B`` (reference: trnsparse/ops.py:162-210).
+
+    Output has A's dtype; rows of empty block-rows are zero. One column
+    (``B`` of shape (n, 1)) runs the HBM-bound BSR SpMV kernel; block size
+    128 runs the tensor-core kernel; other block sizes run the CUDA-core
+    kernel.
+    """
+    m, n = A.shape
+    if B.shape[0] != n:
+        raise AssertionError(f"Dimension mismatch: A is {A.shape}, B is {tuple(B.shape)}")
+    k = B.shape[1]
+    dev = _dev_of(B)
+    if A.dtype != torch.float32:
+        raise TypeError(f"bsr_spmm: blocks dtype {A.dtype} not supported (float32, bfloat16)")
+    Bd = _on(B, dev, torch.float32)
+    out = torch.empty(m, k, dtype=A.dtype, device=dev)
+    geo = _bsr_geometry(A, dev)
+    s = _lib.stream_handle(dev)
+    with torch.cuda.device(dev):
+        if k == 1:
+            _lib.call("trnsparse_bsr_spmv", *geo, Bd.data_ptr(), 1.0, None, 0.0, out.data_ptr(), s)
+        else:
+            _lib.call("trnsparse_bsr_spmm_simt", *geo, Bd.data_ptr(), k, k, out.data_ptr(), k, s)
+    return _back(out, B)
