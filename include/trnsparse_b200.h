@@ -159,6 +159,24 @@ TRNSPARSE_API int trnsparse_bsr_spmm_simt(int64_t m, int64_t n, int b, int64_t n
                             const int* col_idx, const float* blocks, const float* B, int64_t k,
                             int64_t ldb, float* C, int64_t ldc, void* stream);
 
+/* Allocation-free PCG. No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory (code running inside an
+ * allocator or pool callback, or hosts with a fixed up-front memory budget).
+ * Runs the same solve as trnsparse_bsr_cg_start + trnsparse_bsr_cg_iterate
+ * over [0, max_iter + 1), but its scratch is a fixed 64 MiB array inside the
+ * library, held on every GPU that loads the library until exit, instead of a
+ * caller workspace; sizes whose trnsparse_bsr_cg_workspace_size exceeds that
+ * are rejected with TRNSPARSE_ERR_ARG. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. All calls share the one array, so calls that
+ * overlap on the GPU (other streams, other host threads) race; run them one
+ * after another. status_out (nullable, device, 64 bytes) receives the final
+ * status record described above. Calls no allocating routine. */
+TRNSPARSE_API int trnsparse_bsr_cg_noalloc(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                             const int* col_idx, const float* blocks, const float* b_vec, float* x,
+                             int x_is_zero, const float* inv_d, double tol, int max_iter,
+                             void* status_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
