@@ -159,6 +159,28 @@ TRNSPARSE_API int trnsparse_bsr_spmm_simt(int64_t m, int64_t n, int b, int64_t n
                             const int* col_idx, const float* blocks, const float* B, int64_t k,
                             int64_t ldb, float* C, int64_t ldc, void* stream);
 
+/* C = A @ B on the tensor cores (tcgen05.mma, TMA, TMEM), block size 128
+ * only: the hot path of the reference's bsr_spmm (trnsparse/ops.py:195-210)
+ * that nki_bsr_spmm replaces on Trainium (trnsparse/nki/dispatch.py:372-381).
+ *   dtype F32: 3xTF32 (hi*hi + hi*lo + lo*hi); blocks_hi/blocks_lo are the
+ *              tf32 split of the blocks (trnsparse_bsr_split_tf32); B, C fp32.
+ *   dtype BF16: blocks_hi and B are bf16 (blocks_lo unused); C is fp32.
+ * units: int32 triples (block_row, first_block, end_block) covering every
+ * stored block exactly once, each within one block-row; n_units of them.
+ * C (m x k, row stride ldc) is overwritten. bn: N tile (128 or 256; 0 =
+ * choose). Workspace: trnsparse_bsr_spmm_tc_workspace_size(n, k, dtype)
+ * bytes (B transposed to K-major, split for F32). */
+TRNSPARSE_API size_t trnsparse_bsr_spmm_tc_workspace_size(int64_t n, int64_t k, int dtype);
+TRNSPARSE_API int trnsparse_bsr_spmm_tc(int64_t m, int64_t n, int64_t n_blocks, const int* col_idx,
+                          const void* blocks_hi, const void* blocks_lo, int dtype, const int* units,
+                          int n_units, const void* B, int64_t k, int64_t ldb, float* C, int64_t ldc,
+                          int bn, void* ws, size_t ws_bytes, void* stream);
+
+/* hi = tf32(src), lo = tf32(src - hi), elementwise over `count` floats
+ * (round to nearest, ties away). Used once per BSR matrix for the F32
+ * tensor-core path. */
+TRNSPARSE_API int trnsparse_bsr_split_tf32(int64_t count, const float* src, float* hi, float* lo, void* stream);
+
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an
  * allocator or pool callback, or hosts with a fixed up-front memory budget).

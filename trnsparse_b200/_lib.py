@@ -47,12 +47,16 @@ SIGNATURES.update({
     "trnsparse_bsr_power_iterate": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _sz, _p],
     "trnsparse_bsr_power_finish": [_i64, _p, _i32, _p, _p],
     "trnsparse_bsr_spmm_simt": _BSR + [_p, _i64, _i64, _p, _i64, _p],
+    "trnsparse_bsr_spmm_tc_workspace_size": [_i64, _i64, _i32],
+    "trnsparse_bsr_spmm_tc": [_i64, _i64, _i64, _p, _p, _p, _i32, _p, _i32, _p, _i64, _i64, _p, _i64, _i32, _p, _sz, _p],
+    "trnsparse_bsr_split_tf32": [_i64, _p, _p, _p, _p],
     "trnsparse_bsr_cg_noalloc": _BSR + [_p, _p, _i32, _p, _f64, _i32, _p, _p],
 })
 _RESTYPE = {
     "trnsparse_last_error": C.c_char_p,
     "trnsparse_bsr_cg_workspace_size": C.c_size_t,
     "trnsparse_bsr_power_workspace_size": C.c_size_t,
+    "trnsparse_bsr_spmm_tc_workspace_size": C.c_size_t,
 }
 
 _lib = None

@@ -19,6 +19,7 @@ enum DeviceError : int {
   DEVERR_MBAR_TIMEOUT = 1,
   DEVERR_TMEM_ALLOC = 2,
   DEVERR_PEER_TIMEOUT = 3,
+  DEVERR_SELFCHECK_SMEM = 4,  // a shared-memory tile failed its alignment self-check
 };
 
 constexpr uint32_t kSpinLimit = 1u << 26;

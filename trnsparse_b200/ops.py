@@ -191,28 +191,102 @@ def _bsr_geometry(A: BSRMatrix, dev: torch.device, dtype: torch.dtype = torch.fl
     return (m, n, A.block_size, A.n_blocks, lay["row_ptr"].data_ptr(), lay["col_idx"].data_ptr(), blocks.data_ptr())
 
 
+def _sm_count(dev: torch.device) -> int:
+    return torch.cuda.get_device_properties(dev).multi_processor_count
+
+
+def _tc_plan(A: BSRMatrix, lay: dict, dev: torch.device, k: int) -> tuple[torch.Tensor, int, int]:
+    """Work units (block_row, first, end) for the tensor-core kernel, cached per N tiling.
+
+    The N tile is 128 or 256 columns; the stored blocks of a block-row are
+    split into runs of G blocks, with G chosen so the grid covers the SMs
+    about once (each CTA holds one SM: ~193 KB of shared memory).
+    """
+    sms = _sm_count(dev)
+    bn = 128 if k <= 128 else 256
+    if bn == 256 and A.n_blocks * (-(-k // 256)) < sms:
+        bn = 128  # narrower tiles give a small problem more CTAs
+    n_tiles = -(-k // bn)
+    key = ("tc_units", bn)
+    hit = lay.get(key)
+    if hit is not None:
+        return hit
+    G = max(1, round(A.n_blocks * n_tiles / sms))
+    rp = lay["host_row_ptr"].tolist()
+    units = [(i, s, min(s + G, rp[i + 1])) for i in range(len(rp) - 1) for s in range(rp[i], rp[i + 1], G)]
+    t = torch.tensor(units, dtype=torch.int32).reshape(-1, 3).to(dev)
+    lay[key] = (t, len(units), bn)
+    return lay[key]
+
+
+def _tf32_split(lay: dict, dev: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    hit = lay.get("tf32_split")
+    if hit is None:
+        blocks = lay["blocks"]
+        if blocks.dtype != torch.float32:
+            blocks = blocks.float().contiguous()
+        hi = torch.empty_like(blocks)
+        lo = torch.empty_like(blocks)
+        with torch.cuda.device(dev):
+            _lib.call("trnsparse_bsr_split_tf32", blocks.numel(), blocks.data_ptr(), hi.data_ptr(), lo.data_ptr(),
+                      _lib.stream_handle(dev))
+        hit = lay["tf32_split"] = (hi, lo)
+    return hit
+
+
 def bsr_spmm(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
     """``C = A @ B`` for a BSR ``A`` and dense ``B`` (reference: trnsparse/ops.py:162-210).
 
-    Output has A's dtype; rows of empty block-rows are zero. One column
-    (``B`` of shape (n, 1)) runs the HBM-bound BSR SpMV kernel; block size
-    128 runs the tensor-core kernel; other block sizes run the CUDA-core
-    kernel.
+    The result has A's dtype; rows of empty block-rows are zero. Paths, all
+    on the GPU: one right-hand-side column runs the HBM-bound BSR SpMV
+    kernel; block size 128 runs the tcgen05 tensor-core kernel (3xTF32 for
+    float32, bf16 operands with fp32 accumulation for bfloat16); other block
+    sizes run the CUDA-core kernel (float32 FMA).
     """
     m, n = A.shape
     if B.shape[0] != n:
         raise AssertionError(f"Dimension mismatch: A is {A.shape}, B is {tuple(B.shape)}")
     k = B.shape[1]
     dev = _dev_of(B)
-    if A.dtype != torch.float32:
+    if A.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"bsr_spmm: blocks dtype {A.dtype} not supported (float32, bfloat16)")
-    Bd = _on(B, dev, torch.float32)
-    out = torch.empty(m, k, dtype=A.dtype, device=dev)
-    geo = _bsr_geometry(A, dev)
     s = _lib.stream_handle(dev)
+    lay = A.device_layout(dev)
     with torch.cuda.device(dev):
+        if A.block_size == 128 and k > 1 and A.n_blocks > 0:
+            bf16 = A.dtype == torch.bfloat16
+            Bd = _on(B, dev, torch.bfloat16 if bf16 else torch.float32)
+            out = torch.empty(m, k, dtype=torch.float32, device=dev)
+            units, n_units, bn = _tc_plan(A, lay, dev, k)
+            if bf16:
+                (hi, lo), code = (lay["blocks"], None), _lib.BF16
+            else:
+                (hi, lo), code = _tf32_split(lay, dev), _lib.F32
+            ws_bytes = _lib.raw("trnsparse_bsr_spmm_tc_workspace_size")(n, k, code)
+            ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+            _lib.call("trnsparse_bsr_spmm_tc", m, n, A.n_blocks, lay["col_idx"].data_ptr(), hi.data_ptr(),
+                      _lib.ptr(lo), code, units.data_ptr(), n_units, Bd.data_ptr(), k, k, out.data_ptr(), k, bn,
+                      ws.data_ptr(), ws_bytes, s)
+            return _back(out.to(A.dtype) if bf16 else out, B)
+        Bd = _on(B, dev, torch.float32)
+        out = torch.empty(m, k, dtype=torch.float32, device=dev)
+        geo = _bsr_geometry(A, dev)
         if k == 1:
             _lib.call("trnsparse_bsr_spmv", *geo, Bd.data_ptr(), 1.0, None, 0.0, out.data_ptr(), s)
         else:
             _lib.call("trnsparse_bsr_spmm_simt", *geo, Bd.data_ptr(), k, k, out.data_ptr(), k, s)
+    return _back(out.to(A.dtype), B)
+
+
+def bsr_spmm_cuda_core(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
+    """``A @ B`` on the CUDA-core kernel (fp32 FMA): a second, independent
+    device implementation used to cross-check the tensor-core path."""
+    m, n = A.shape
+    dev = _dev_of(B)
+    Bd = _on(B, dev, torch.float32)
+    out = torch.empty(m, B.shape[1], dtype=torch.float32, device=dev)
+    geo = _bsr_geometry(A, dev)
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_bsr_spmm_simt", *geo, Bd.data_ptr(), B.shape[1], B.shape[1], out.data_ptr(),
+                  B.shape[1], _lib.stream_handle(dev))
     return _back(out, B)
