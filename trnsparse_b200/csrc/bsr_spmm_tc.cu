@@ -11,7 +11,7 @@
 // issues TMA loads of the A and B^T chunks into a ring of shared-memory
 // stages, warp 1 issues tcgen05.mma into a 128 x BN fp32 accumulator in
 // TMEM, and all four warps drain TMEM with tcgen05.ld and add the tile into
-// C (float4 atomics; C is zeroed first, so units that split a block-row
+// C (red.global.add.v4 reductions; C is zeroed first, so units that split a block-row
 // combine). No host-side gather or K_max padding of B (the reference's NKI
 // path materialises B once per block).
 //
@@ -51,6 +51,28 @@ inline int debug_sync(cudaStream_t st, const char* step) {
   return TRNSPARSE_OK;
 }
 
+// Fire-and-forget float adds into global memory (no returned value to wait on).
+__device__ __forceinline__ void red_add_v4(float* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(p), "f"(__uint_as_float(a)),
+               "f"(__uint_as_float(b)), "f"(__uint_as_float(c)), "f"(__uint_as_float(d))
+               : "memory");
+}
+__device__ __forceinline__ void red_add(float* p, uint32_t a) {
+  asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(p), "f"(__uint_as_float(a)) : "memory");
+}
+
+#ifdef TSB_TC_TRACE
+__device__ unsigned long long g_tc_trace[1024][8];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define TC_TRACE(slot) g_tc_trace[(blockIdx.x + blockIdx.y * gridDim.x) & 1023][slot] = gtime()
+#else
+#define TC_TRACE(slot)
+#endif
+
 template <MmaKind KIND>
 struct TcCfg {
   static constexpr int kElem = KIND == MmaKind::TF32 ? 4 : 2;
@@ -68,6 +90,7 @@ struct TcLayout {
   static constexpr int kStage = TcCfg<KIND>::kParts * (kATile + kBTile);
   static constexpr int kStages = kSmemBudget / kStage;
   static constexpr int kSmem = kStages * kStage + 1024;
+  static_assert(kStages * kStage >= 128 * (BN + 4) * 4, "epilogue tile must fit in the operand ring");
 };
 
 template <MmaKind KIND, int BN>
@@ -94,6 +117,7 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
     return sbase + s * Lay::kStage + Cfg::kParts * Lay::kATile + part * Lay::kBTile;
   };
 
+  if (threadIdx.x == 0) TC_TRACE(0);
   const int warp = threadIdx.x >> 5;
   const int row_blk = units[3 * blockIdx.x + 0];
   const int blk0 = units[3 * blockIdx.x + 1];
@@ -125,6 +149,7 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  if (threadIdx.x == 0) TC_TRACE(1);
 
   if (warp == 0 && elect_lane0()) {
     // ---------------- TMA producer
@@ -147,6 +172,7 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
         tma_load_2d(b_tile(s, 1), &tb_lo, j * 128 + c * Cfg::kChunk, n0, &full_bar[s]);
       }
       issued = it + 1;
+      if (it == 0) TC_TRACE(2);
     }
     // never leave the CTA with copies in flight: on the abort path wait for
     // every issued fill the consumer has not waited for
@@ -165,6 +191,7 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
         break;
       }
       tc_fence_after();
+      if (it == 0) TC_TRACE(3);
       const uint32_t ah = smem_u32(a_tile(s, 0)), bh = smem_u32(b_tile(s, 0));
 #pragma unroll
       for (int ks = 0; ks < Cfg::kSteps; ++ks) {
@@ -180,41 +207,62 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
       umma_commit(&empty_bar[s]);
     }
     umma_commit(&done_bar);
+    TC_TRACE(4);
   }
   __syncwarp();
 
   // ---------------- epilogue: TMEM -> registers -> C (all 4 warps)
   const bool ok = mbar_wait(&done_bar, 0);
   tc_fence_after();
-  if (ok && !*(volatile int*)&abort_flag && total > 0) {
+  if (threadIdx.x == 0) TC_TRACE(5);
+  // Each warp moves its 32 accumulator rows TMEM -> registers -> a padded
+  // shared-memory tile (the operand ring is idle now); then the CTA adds the
+  // tile into C with coalesced 16-byte reductions, a warp covering 512
+  // contiguous bytes of a row per instruction.
+  const bool run = ok && !*(volatile int*)&abort_flag && total > 0;
+  constexpr int LDS = BN + 4;  // padded row stride (floats): conflict-free float4 stores
+  float* stile = reinterpret_cast<float*>(sbase);
+  if (run) {
     const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(row_blk) * 128 + warp * 32 + lane;
-    float* crow = C + row * ldc;
-    const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    const int r_local = warp * 32 + lane;
 #pragma unroll 1
     for (int cc = 0; cc < BN / 32; ++cc) {
       uint32_t r[32];
       tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + cc * 32, r);
       tmem_wait_ld();
-      const int64_t col0 = n0 + cc * 32;
-      if (row < m && col0 < k) {
-        if (vec && col0 + 32 <= k) {
+      float4* dst = reinterpret_cast<float4*>(stile + r_local * LDS + cc * 32);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-            atomicAdd(reinterpret_cast<float4*>(crow + col0 + 4 * q), v);
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q)
-            if (col0 + q < k) atomicAdd(crow + col0 + q, __uint_as_float(r[q]));
+      for (int q = 0; q < 8; ++q)
+        dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                             __uint_as_float(r[4 * q + 3]));
+    }
+  }
+  __syncthreads();
+  if (run) {
+    const int64_t row0 = static_cast<int64_t>(row_blk) * 128;
+    const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (n0 + BN <= k);
+    if (vec) {
+      constexpr int F4 = BN / 4;  // float4 per tile row
+      for (int f = threadIdx.x; f < 128 * F4; f += kTcThreads) {
+        const int rl = f / F4, c4 = f - rl * F4;
+        const int64_t row = row0 + rl;
+        if (row < m) {
+          const float4 v = *reinterpret_cast<const float4*>(stile + rl * LDS + 4 * c4);
+          red_add_v4(C + row * ldc + n0 + 4 * c4, __float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z),
+                     __float_as_uint(v.w));
         }
+      }
+    } else {
+      for (int f = threadIdx.x; f < 128 * BN; f += kTcThreads) {
+        const int rl = f / BN, c = f - rl * BN;
+        const int64_t row = row0 + rl, col = n0 + c;
+        if (row < m && col < k) red_add(C + row * ldc + col, __float_as_uint(stile[rl * LDS + c]));
       }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TC_TRACE(6);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, BN);
@@ -390,3 +438,9 @@ extern "C" int trnsparse_bsr_spmm_tc(int64_t m, int64_t n, int64_t n_blocks, con
   return bn == 128 ? launch_tc<MmaKind::BF16, 128>(ahi, alo, bhi, blo, units, n_units, col_idx, m, k, C, ldc, st)
                    : launch_tc<MmaKind::BF16, 256>(ahi, alo, bhi, blo, units, n_units, col_idx, m, k, C, ldc, st);
 }
+
+#ifdef TSB_TC_TRACE
+extern "C" __attribute__((visibility("default"))) int trnsparse_tc_trace_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, tsb::g_tc_trace, sizeof(tsb::g_tc_trace));
+}
+#endif

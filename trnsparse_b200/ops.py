@@ -203,9 +203,7 @@ def _tc_plan(A: BSRMatrix, lay: dict, dev: torch.device, k: int) -> tuple[torch.
     about once (each CTA holds one SM: ~193 KB of shared memory).
     """
     sms = _sm_count(dev)
-    bn = 128 if k <= 128 else 256
-    if bn == 256 and A.n_blocks * (-(-k // 256)) < sms:
-        bn = 128  # narrower tiles give a small problem more CTAs
+    bn = 128 if k <= 128 else 256  # wide tiles read each A block once per 256 columns
     n_tiles = -(-k // bn)
     key = ("tc_units", bn)
     hit = lay.get(key)
