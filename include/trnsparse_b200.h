@@ -181,6 +181,24 @@ TRNSPARSE_API int trnsparse_bsr_spmm_tc(int64_t m, int64_t n, int64_t n_blocks, 
  * tensor-core path. */
 TRNSPARSE_API int trnsparse_bsr_split_tf32(int64_t count, const float* src, float* hi, float* lo, void* stream);
 
+/* C = (A o mask) @ B with the Schwarz screening mask applied inside the
+ * tensor-core kernel (3xTF32, fp32 in/out): the reference's screened_spmm
+ * (trnsparse/ops.py:213-277; nki_screened_spmm, trnsparse/nki/dispatch.py:
+ * 487-494, kernels.py:86-155). A is M x K (row stride lda), B is K x N
+ * (ldb), C is M x N (ldc), all row-major fp32; lda, ldq multiples of 4.
+ *   bounds_kind 1: `bounds` is the length-M diag_integrals vector (M == K);
+ *                  mask[i,j] = sqrt|d_i| * sqrt|d_j| > fp32(sqrt(threshold)).
+ *   bounds_kind 2: `bounds` is the M x K pair-bound matrix Q (row stride ldq)
+ *                  of screening.py's schwarz_bounds; mask = Q > fp32(sqrt(thr))
+ *                  (screen_quartets, screening.py:29-40).
+ * K chunks with no surviving pair issue no MMA. Workspace:
+ * trnsparse_screened_spmm_workspace_size(K, N) bytes (B^T split). */
+TRNSPARSE_API size_t trnsparse_screened_spmm_workspace_size(int64_t K, int64_t N);
+TRNSPARSE_API int trnsparse_screened_spmm(int64_t M, int64_t K, int64_t N, const float* A, int64_t lda,
+                            const float* bounds, int bounds_kind, int64_t ldq, double threshold,
+                            const float* B, int64_t ldb, float* C, int64_t ldc, void* ws,
+                            size_t ws_bytes, void* stream);
+
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an
  * allocator or pool callback, or hosts with a fixed up-front memory budget).

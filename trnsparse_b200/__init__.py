@@ -23,6 +23,7 @@ from .iterative import (
 from .ops import (
     bsr_spmm,
     nnz_per_row,
+    screened_spmm,
     sparse_add,
     sparse_scale,
     sparse_transpose,
@@ -43,6 +44,7 @@ __all__ = [
     "spmm",
     "spmv_symmetric",
     "bsr_spmm",
+    "screened_spmm",
     "sparse_add",
     "sparse_scale",
     "sparse_transpose",

@@ -26,40 +26,13 @@
 // starts 16 bytes into the window), so it is declared 16-byte aligned and the
 // 1024-byte alignment the 128-byte-swizzled TMA tiles need is done by hand; an
 // over-aligned declaration would let the compiler fold that round-up away.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-#include <stdlib.h>
-
-#include "common.cuh"
-#include "tc.cuh"
+#include "tc_common.cuh"
 
 namespace tsb {
 namespace {
 
 constexpr int kTcThreads = 128;
 constexpr int kSmemBudget = 200 * 1024;
-
-// TRNSPARSE_DEBUG_SYNC=1: synchronise after each launch and name the step that failed.
-inline int debug_sync(cudaStream_t st, const char* step) {
-  static const int on = [] {
-    const char* v = getenv("TRNSPARSE_DEBUG_SYNC");
-    return (v && *v == '1') ? 1 : 0;
-  }();
-  if (!on) return TRNSPARSE_OK;
-  cudaError_t e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) return cuda_status(e, step);
-  return TRNSPARSE_OK;
-}
-
-// Fire-and-forget float adds into global memory (no returned value to wait on).
-__device__ __forceinline__ void red_add_v4(float* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(p), "f"(__uint_as_float(a)),
-               "f"(__uint_as_float(b)), "f"(__uint_as_float(c)), "f"(__uint_as_float(d))
-               : "memory");
-}
-__device__ __forceinline__ void red_add(float* p, uint32_t a) {
-  asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(p), "f"(__uint_as_float(a)) : "memory");
-}
 
 #ifdef TSB_TC_TRACE
 __device__ unsigned long long g_tc_trace[1024][8];
@@ -269,56 +242,6 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
   }
 }
 
-// ---------------------------------------------------------------- prep kernels
-__device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-__global__ void split_tf32_kernel(int64_t n, const float* __restrict__ src, float* __restrict__ hi,
-                                  float* __restrict__ lo) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float x = src[i];
-    const float h = tf32_rna(x);
-    hi[i] = h;
-    lo[i] = tf32_rna(x - h);
-  }
-}
-
-// Bt[kk][nn] = B[nn][kk] for nn < n, 0 for n <= nn < n_pad (32x32 smem tiles).
-// SPLIT (fp32): writes the tf32 hi/lo split; otherwise a plain bf16 transpose.
-template <bool SPLIT, typename E>
-__global__ void transpose_b_kernel(int64_t n, int64_t k, const E* __restrict__ B, int64_t ldb, int64_t n_pad,
-                                   E* __restrict__ hi, E* __restrict__ lo) {
-  __shared__ float tile[32][33];
-  const int64_t nb = static_cast<int64_t>(blockIdx.x) * 32, kb = static_cast<int64_t>(blockIdx.y) * 32;
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int64_t nn = nb + r, kk = kb + threadIdx.x;
-    float v = 0.f;
-    if (nn < n && kk < k) {
-      if constexpr (sizeof(E) == 4) v = B[nn * ldb + kk];
-      else v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(B + nn * ldb + kk));
-    }
-    tile[r][threadIdx.x] = v;
-  }
-  __syncthreads();
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int64_t kk = kb + r, nn = nb + threadIdx.x;
-    if (kk < k && nn < n_pad) {
-      const float v = tile[threadIdx.x][r];
-      if constexpr (SPLIT) {
-        const float h = tf32_rna(v);
-        hi[kk * n_pad + nn] = h;
-        lo[kk * n_pad + nn] = tf32_rna(v - h);
-      } else {
-        *reinterpret_cast<__nv_bfloat16*>(hi + kk * n_pad + nn) = __float2bfloat16_rn(v);
-      }
-    }
-  }
-}
-
 template <MmaKind KIND, int BN>
 int launch_tc(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
               const int* units, int n_units, const int* col_idx, int64_t m, int64_t k, float* C, int64_t ldc,
@@ -331,32 +254,6 @@ int launch_tc(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap&
   kern<<<grid, kTcThreads, Lay::kSmem, st>>>(ahi, alo, bhi, blo, units, col_idx, m, k, C, ldc);
   TSB_CHECK_LAUNCH("bsr_spmm_tc launch");
   return debug_sync(st, "bsr_spmm_tc: main kernel (sync)");
-}
-
-inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
-
-int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
-                 uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows) {
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  if (!encode) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
-      return fail(TRNSPARSE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (row_bytes & 15u))
-    return fail(TRNSPARSE_ERR_ALIGN, "tensor map: base/stride not 16-byte aligned");
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_cols, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(TRNSPARSE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return TRNSPARSE_OK;
 }
 
 }  // namespace

@@ -288,3 +288,64 @@ def bsr_spmm_cuda_core(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
         _lib.call("trnsparse_bsr_spmm_simt", *geo, Bd.data_ptr(), B.shape[1], B.shape[1], out.data_ptr(),
                   B.shape[1], _lib.stream_handle(dev))
     return _back(out, B)
+
+
+# ---------------------------------------------------------------------------
+# Screened SpMM
+# ---------------------------------------------------------------------------
+
+
+def screened_spmm(
+    A: torch.Tensor,
+    diag_integrals: torch.Tensor,
+    B: torch.Tensor,
+    threshold: float,
+) -> torch.Tensor:
+    """``C = (A * mask) @ B`` with the Schwarz mask applied inside the kernel
+    (reference: trnsparse/ops.py:213-277).
+
+    1-D ``diag_integrals`` (the reference's signature, square A):
+    ``Q = sqrt(|d|)``, ``mask[i,j] = Q[i]*Q[j] > sqrt(threshold)``.
+    2-D ``diag_integrals`` (extension): the already-computed pair bounds
+    ``Q = schwarz_bounds(G)``; ``mask = screen_quartets(Q, threshold)``,
+    i.e. ``Q > sqrt(threshold)`` (trnsparse/screening.py:29-40).
+    Comparisons are in float32, like the reference's tensor comparisons.
+    """
+    M, K = A.shape
+    if diag_integrals.dim() == 1:
+        assert diag_integrals.shape[0] == M == K, (
+            "screened_spmm requires square A with diag_integrals of matching length; "
+            f"got A shape {A.shape}, diag_integrals shape {diag_integrals.shape}"
+        )
+        kind = 1
+    else:
+        assert diag_integrals.dim() == 2 and tuple(diag_integrals.shape) == (M, K), (
+            f"2-D bounds must match A: got {tuple(diag_integrals.shape)} for A {tuple(A.shape)}"
+        )
+        kind = 2
+    assert B.shape[0] == K, f"Dimension mismatch: A is {tuple(A.shape)}, B is {tuple(B.shape)}"
+    if A.dtype != torch.float32:
+        raise TypeError(f"screened_spmm: dtype {A.dtype} not supported (float32)")
+    N = B.shape[1]
+    dev = _dev_of(A, B, diag_integrals)
+    Ad = _on(A, dev, torch.float32)
+    Qd = _on(diag_integrals, dev, torch.float32)
+    Bd = _on(B, dev, torch.float32)
+    if K % 4 or Ad.data_ptr() % 16 or Qd.data_ptr() % 16:
+        # TMA needs 16-byte row strides and bases: pad K to a multiple of 4 with zero columns
+        Kp = -(-K // 4) * 4
+        Ap = torch.zeros(M, Kp, device=dev)
+        Ap[:, :K] = Ad
+        Ad = Ap
+        if kind == 2:
+            Qp = torch.zeros(M, Kp, device=dev)
+            Qp[:, :K] = Qd
+            Qd = Qp
+    out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    ws_bytes = _lib.raw("trnsparse_screened_spmm_workspace_size")(K, N)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_screened_spmm", M, K, N, Ad.data_ptr(), Ad.shape[1], Qd.data_ptr(), kind,
+                  Qd.shape[-1] if kind == 2 else 0, float(threshold), Bd.data_ptr(), N, out.data_ptr(), N,
+                  ws.data_ptr(), ws_bytes, _lib.stream_handle(dev))
+    return _back(out, B)
