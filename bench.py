@@ -268,7 +268,108 @@ def run_ours(args, ws, rank, local):
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_spmv(A, x_host)
+    if rank == 0 and ws == 1 and not args.no_extra:
+        line["extra"] = run_extras(pk, flush)
     return line
+
+
+def time_call(f, reps: int, flush: L2Flush | None) -> float:
+    """Median device milliseconds of one call of ``f`` replayed from a CUDA
+    graph; with ``flush`` the L2 is flushed (outside the timed window) before
+    every replay, for workloads whose inputs fit in L2."""
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        f()
+        with torch.cuda.graph(g, stream=s):
+            f()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        if flush:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(b))
+    out.sort()
+    return out[len(out) // 2]
+
+
+def run_extras(pk: dict, flush: L2Flush) -> dict:
+    """Secondary rows: the other benchmark configurations, one call each.
+
+    bsr_spmm / screened_spmm: nonzero-block FLOP/s (2*128*128*k per stored
+    block; fp32 runs 3xTF32, i.e. three tensor-core passes per FLOP counted).
+    Peaks: bf16 = measured cuBLAS burst; tf32 = bf16 x 0.5 (the B200 spec
+    ratio of dense TF32 to BF16), so fp32 3xTF32 tops out near 1/6 of bf16.
+    """
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+
+    tf32 = 0.5 * pk["bf16_tflops"]
+    ex = {}
+    # config 1 and a scaled variant with the same distribution
+    for name, grid, k in [("config1_bsr_spmm", 16, 256), ("bsr_spmm_grid128_k512", 128, 512)]:
+        for dt, tag in [(torch.float32, "f32_3xtf32"), (torch.bfloat16, "bf16")]:
+            A, B = w.bsr_random_grid(grid=grid, k=k, dtype=dt)
+            Bd = B.cuda()
+            small = grid == 16
+            ms = time_call(lambda: ts.bsr_spmm(A, Bd), 20, flush if small else None)
+            tfl = 2 * 128 * 128 * k * A.n_blocks / (ms * 1e-3) / 1e12
+            peak = pk["bf16_tflops"] if dt == torch.bfloat16 else tf32 / 3
+            ex[f"{name}_{tag}"] = {"TFLOP/s": round(tfl, 1), "ms": round(ms, 4), "n_blocks": A.n_blocks,
+                                   "frac_of_peak": round(tfl / peak, 3),
+                                   "peak": ("bf16 measured" if dt == torch.bfloat16 else "tf32 derived / 3 passes"),
+                                   "l2": "flushed" if small else "inputs exceed L2",
+                                   "includes": "zeroing C, B transpose/split, tensor-core kernel"}
+            del A, B, Bd
+    # config 2b: CSR spmm, k = 32
+    A = w.poisson2d_csr(2048)
+    Bm = w.poisson_rhs(A.shape[0], 32).cuda()
+    n = A.shape[0]
+    ms = time_call(lambda: ts.spmm(A, Bm), 10, None)
+    nb = 8 * A.nnz + 4 * (n + 1) + 4 * n * 32 * 2
+    ex["config2b_csr_spmm_k32"] = {"GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
+                                   "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
+    del Bm
+    # config 3: screened_spmm with 2-D pair bounds
+    Af, Qf, Bf, _, thr = w.fock_like()
+    Ad, Qd, Bd = Af.cuda(), Qf.cuda(), Bf.cuda()
+    del Af, Qf, Bf
+    ms = time_call(lambda: ts.screened_spmm(Ad, Qd, Bd, thr), 10, None)
+    fl = 2 * 8192 * 8192 * 512  # every 128x128 block has a surviving pair (unsorted centres)
+    ex["config3_screened_spmm"] = {"TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4),
+                                   "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / (tf32 / 3), 3),
+                                   "peak": "tf32 derived / 3 passes"}
+    del Ad, Qd, Bd
+    # config 5: Jacobi-PCG, 200 iterations, tol 0
+    A5, b5 = w.block_pentadiagonal_spd()
+    M5 = ts.jacobi_preconditioner_bsr(A5)
+    bd = b5.cuda()
+    ts.cg_bsr(A5, bd, tol=0.0, max_iter=5, M=M5)
+    torch.cuda.synchronize()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    x, it, rel = ts.cg_bsr(A5, bd, tol=0.0, max_iter=200, M=M5)
+    e.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(e)
+    ex["config5_cg_bsr_jacobi_200"] = {"ms_total": round(ms, 3), "iters_reported": it, "rel_residual": rel,
+                                       "note": "reference semantics stop the work when |p.Ap| < 1e-30 (reported "
+                                               "iters stays max_iter); see bsr_spmv row for per-iteration cost"}
+    xv = bd.unsqueeze(1)
+    ms = time_call(lambda: ts.bsr_spmm(A5, xv), 10, None)
+    nb = A5.n_blocks * 128 * 128 * 4 + 4 * A5.n_blocks + 4 * 2049 + 8 * A5.shape[0]
+    ex["config5_bsr_spmv"] = {"GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
+                              "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
+    return ex
 
 
 def cpu_baseline_spmv(A, x_host, budget_s: float = 3.0) -> dict:
@@ -324,6 +425,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the secondary configurations")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
