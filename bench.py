@@ -263,7 +263,8 @@ def run_ours(args, ws, rank, local):
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(ach / pk["hbm_gbs"], 4), "peak_source": pk["source"] + " (burst copy)",
-                     "traffic": None, "kernel": "csr_spmv_warp_kernel<int,float,2,384>"},
+                     "traffic": 205.3e6, "traffic_source": "ncu dram__bytes_read+write, one cold launch "
+                     "(profiles/csr_spmv_warp_config2.md)", "kernel": "csr_spmv_warp_kernel<int,float,2,384>"},
         "clocks": clk.summary(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
