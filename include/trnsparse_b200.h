@@ -199,6 +199,19 @@ TRNSPARSE_API int trnsparse_screened_spmm(int64_t M, int64_t K, int64_t N, const
                             const float* B, int64_t ldb, float* C, int64_t ldc, void* ws,
                             size_t ws_bytes, void* stream);
 
+/* Block-sparse attention forward: O = softmax(Q K^T * scale) V restricted to
+ * the stored blocks of a BSR mask (pattern only), per head: the reference's
+ * block_sparse_attention_tiled (trnsparse/ops.py:549-625; two-pass CPU form
+ * ops.py:280-357; nki_bsr_attn_tiled, trnsparse/nki/dispatch.py:580).
+ * Q, K, V, O: heads contiguous (heads, seq, head_dim) row-major tensors of
+ * `dtype` (F32 or BF16); softmax and accumulation in fp32. The mask has
+ * seq/block_size block-rows; rows of an empty block-row, and rows past the
+ * last whole block, are zero. head_dim <= 256. */
+TRNSPARSE_API int trnsparse_bsr_attention(int64_t heads, int64_t seq, int64_t head_dim, int block_size,
+                            const int* block_row_ptr, const int* block_col_idx, const void* Q,
+                            const void* K, const void* V, void* O, int dtype, double scale,
+                            void* stream);
+
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an
  * allocator or pool callback, or hosts with a fixed up-front memory budget).

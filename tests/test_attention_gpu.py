@@ -1,0 +1,89 @@
+"""block_sparse_attention_tiled on the GPU against the reference's golden
+outputs and the CPU oracle.
+
+fp32: atol/rtol 1e-4 (the reference's own tiled-vs-naive tolerance,
+tests/test_attention.py:96-148). bf16 I/O with fp32 softmax: 2e-2 relative
+Frobenius error against the oracle on the fp32-upcast inputs.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import oracle
+import trnsparse_b200 as ts
+from trnsparse_b200 import workloads as w
+from conftest import golden_cases, golden_names, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+class _Mask:
+    def __init__(self, rp, ci, b, seq):
+        self.block_row_ptrs, self.block_col_indices, self.block_size, self.shape = rp, ci, b, (seq, seq)
+
+
+@pytest.mark.parametrize("name", golden_names("attention"))
+def test_attention_golden(name):
+    c = golden_cases()[name]
+    seq = c["Q"].shape[0]
+    m = _Mask(c["block_row_ptrs"], c["block_col_indices"], c["block_size"], seq)
+    got = ts.block_sparse_attention_tiled(c["Q"].cuda(), c["K"].cuda(), c["V"].cuda(), m)
+    torch.testing.assert_close(got.cpu(), c["out"], atol=1e-4, rtol=1e-4)
+
+
+def test_attention_host_tensors_and_bsr_mask():
+    c = golden_cases()["attn_local"]
+    mask = ts.BSRMatrix(torch.ones(int(c["block_row_ptrs"][-1]), 128, 128), c["block_col_indices"],
+                        c["block_row_ptrs"], (256, 256), 128)
+    got = ts.block_sparse_attention_tiled(c["Q"], c["K"], c["V"], mask)
+    assert got.device.type == "cpu"
+    torch.testing.assert_close(got, c["out"], atol=1e-4, rtol=1e-4)
+
+
+def test_attention_batched_bf16_sliding_window():
+    heads, seq, hd = 3, 2048, 128
+    mask = w.sliding_window_mask(seq=seq)
+    Q, K, V = w.attention_inputs(heads=heads, seq=seq, hd=hd, seed=3)
+    got = ts.block_sparse_attention_tiled(Q.cuda(), K.cuda(), V.cuda(), mask)
+    assert got.dtype == torch.bfloat16 and got.shape == Q.shape
+    for h in range(heads):
+        ref = oracle.block_sparse_attention(Q[0, h].float(), K[0, h].float(), V[0, h].float(),
+                                            mask.block_row_ptrs, mask.block_col_indices, 128)
+        assert rel_fro(got[0, h].float(), ref) <= 2e-2
+
+
+def test_attention_custom_scale_and_ragged_seq():
+    torch.manual_seed(0)
+    seq, hd, b = 200, 48, 64  # 3 whole blocks, 8 trailing rows outside the mask
+    Q, K, V = (torch.randn(seq, hd) for _ in range(3))
+    rp = torch.tensor([0, 1, 3, 5])
+    ci = torch.tensor([0, 0, 1, 1, 2])
+    m = _Mask(rp, ci, b, seq)
+    got = ts.block_sparse_attention_tiled(Q.cuda(), K.cuda(), V.cuda(), m, scale=0.3).cpu()
+    ref = oracle.block_sparse_attention(Q, K, V, rp, ci, b, scale=0.3)
+    torch.testing.assert_close(got, ref, atol=1e-4, rtol=1e-4)
+    assert torch.count_nonzero(got[192:]) == 0
+
+
+def test_attention_backward_matches_dense_autograd():
+    torch.manual_seed(1)
+    seq, hd, b = 256, 32, 128
+    c = golden_cases()["attn_global"]
+    rp, ci = torch.tensor([0, 1, 3]), torch.tensor([0, 0, 1])
+    m = _Mask(rp, ci, b, seq)
+    Q, K, V = (torch.randn(seq, hd, device="cuda", requires_grad=True) for _ in range(3))
+    out = ts.block_sparse_attention_tiled(Q, K, V, m)
+    g = torch.randn_like(out)
+    out.backward(g)
+    Q2, K2, V2 = (t.detach().clone().requires_grad_(True) for t in (Q, K, V))
+    dense = torch.zeros(seq, seq, dtype=torch.bool, device="cuda")
+    dense[:128, :128] = True
+    dense[128:, :] = True
+    S = (Q2 @ K2.T) * hd**-0.5
+    P = torch.softmax(S.masked_fill(~dense, float("-inf")), dim=-1)
+    (P @ V2).backward(g)
+    for a, r in ((Q.grad, Q2.grad), (K.grad, K2.grad), (V.grad, V2.grad)):
+        torch.testing.assert_close(a, r, atol=1e-4, rtol=1e-4)
+    assert c is not None

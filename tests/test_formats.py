@@ -94,3 +94,15 @@ def test_workload_shapes():
     A5, b5 = w.block_pentadiagonal_spd(8, b=16)
     D = A5.to_dense()
     assert torch.allclose(D, D.T) and torch.linalg.eigvalsh(D.double()).min() > 0
+
+
+def test_public_api_matches_reference_names():
+    """The 30 names of the reference's trnsparse/__init__.py:36-66 are all exported."""
+    ref = ["CSRMatrix", "COOMatrix", "BSRMatrix", "from_dense", "from_scipy", "eye_sparse", "spmv", "spmm",
+           "spmv_symmetric", "bsr_spmm", "screened_spmm", "block_sparse_attention_tiled", "sparse_add",
+           "sparse_scale", "sparse_transpose", "nnz_per_row", "schwarz_bounds", "screen_quartets", "density_screen",
+           "sparsity_stats", "cg_bsr", "chebyshev_bsr", "chebyshev_coeffs", "richardson_bsr", "power_iteration_bsr",
+           "jacobi_preconditioner_bsr", "bsr_diagonal", "HAS_NKI", "set_backend", "get_backend"]
+    assert sorted(ts.__all__) == sorted(ref)
+    for n in ref:
+        assert hasattr(ts, n)

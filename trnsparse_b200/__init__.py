@@ -21,6 +21,7 @@ from .iterative import (
     richardson_bsr,
 )
 from .ops import (
+    block_sparse_attention_tiled,
     bsr_spmm,
     nnz_per_row,
     screened_spmm,
@@ -45,6 +46,7 @@ __all__ = [
     "spmv_symmetric",
     "bsr_spmm",
     "screened_spmm",
+    "block_sparse_attention_tiled",
     "sparse_add",
     "sparse_scale",
     "sparse_transpose",

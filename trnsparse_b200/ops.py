@@ -349,3 +349,105 @@ def screened_spmm(
                   Qd.shape[-1] if kind == 2 else 0, float(threshold), Bd.data_ptr(), N, out.data_ptr(), N,
                   ws.data_ptr(), ws_bytes, _lib.stream_handle(dev))
     return _back(out, B)
+
+
+# ---------------------------------------------------------------------------
+# Block-sparse attention
+# ---------------------------------------------------------------------------
+
+
+def _attn_forward(Q, K, V, mask_bsr, scale):
+    """Device forward for (S, D) or (..., S, D) inputs sharing one mask."""
+    seq, hd = Q.shape[-2], Q.shape[-1]
+    if Q.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"block_sparse_attention_tiled: dtype {Q.dtype} not supported (float32, bfloat16)")
+    dev = _dev_of(Q, K, V)
+    lay = mask_bsr.device_layout(dev) if hasattr(mask_bsr, "device_layout") else None
+    if lay is not None:
+        rp, ci = lay["row_ptr"], lay["col_idx"]
+    else:
+        rp = mask_bsr.block_row_ptrs.to(device=dev, dtype=torch.int32).contiguous()
+        ci = mask_bsr.block_col_indices.to(device=dev, dtype=torch.int32).contiguous()
+    b = mask_bsr.block_size
+    if rp.shape[0] < seq // b + 1:
+        raise AssertionError(f"mask has {rp.shape[0] - 1} block-rows, seq {seq} needs {seq // b}")
+    Qd, Kd, Vd = (_on(t, dev, Q.dtype) for t in (Q, K, V))
+    heads = Qd.numel() // (seq * hd) if seq * hd else 0
+    O = torch.empty_like(Qd)
+    code = _lib.F32 if Q.dtype == torch.float32 else _lib.BF16
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_bsr_attention", heads, seq, hd, b, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
+                  Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), code, float(scale), _lib.stream_handle(dev))
+    return O
+
+
+def _attn_dense_mask(mask_bsr, seq, dev):
+    b = mask_bsr.block_size
+    mt = seq // b
+    rows = torch.repeat_interleave(torch.arange(mt), (mask_bsr.block_row_ptrs[1:mt + 1] - mask_bsr.block_row_ptrs[:mt]).cpu())
+    bm = torch.zeros(mt, mt, dtype=torch.bool)
+    bm[rows, mask_bsr.block_col_indices[: rows.numel()].long().cpu()] = True
+    m = torch.zeros(seq, seq, dtype=torch.bool)
+    m[: mt * b, : mt * b] = bm.repeat_interleave(b, 0).repeat_interleave(b, 1)
+    return m.to(dev)
+
+
+class _AttnFunction(torch.autograd.Function):
+    """Autograd wrapper (reference: ops.py:476-546). Forward runs the CUDA
+    kernel; backward applies the reference's Flash-delta formulas
+    (ops.py:360-473) with dense masked torch ops on the device, which costs
+    O(seq^2) memory and is meant for training-sized problems, not the
+    long-sequence benchmark."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, mask_bsr, scale):
+        O = _attn_forward(Q, K, V, mask_bsr, scale)
+        ctx.save_for_backward(Q, K, V, O)
+        ctx.mask_bsr, ctx.scale = mask_bsr, scale
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, O = ctx.saved_tensors
+        seq = Q.shape[-2]
+        m = _attn_dense_mask(ctx.mask_bsr, seq, Q.device)
+        Qf, Kf, Vf, dOf, Of = (t.float() for t in (Q, K, V, dO.to(Q.device), O))
+        S = (Qf @ Kf.transpose(-1, -2)) * ctx.scale
+        S = S.masked_fill(~m, float("-inf"))
+        mx = S.amax(dim=-1, keepdim=True)
+        mx = torch.where(torch.isfinite(mx), mx, torch.zeros_like(mx))
+        P = torch.exp(S - mx)
+        P = P / P.sum(dim=-1, keepdim=True).clamp(min=1e-12)
+        D = (dOf * Of).sum(dim=-1, keepdim=True)
+        dP = dOf @ Vf.transpose(-1, -2)
+        dS = P * (dP - D)
+        dQ = (dS @ Kf) * ctx.scale
+        dK = (dS.transpose(-1, -2) @ Qf) * ctx.scale
+        dV = P.transpose(-1, -2) @ dOf
+        return dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype), None, None
+
+
+def block_sparse_attention_tiled(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    mask_bsr: BSRMatrix,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Block-sparse softmax attention over the stored blocks of ``mask_bsr``
+    (reference: trnsparse/ops.py:549-625).
+
+    ``Q, K, V``: ``(seq_len, head_dim)`` as in the reference, or with leading
+    batch/head dimensions ``(..., seq_len, head_dim)`` sharing one mask.
+    Only the mask's pattern is used. ``scale`` defaults to
+    ``head_dim ** -0.5``. float32 or bfloat16 in, same dtype out; softmax in
+    float32. Differentiable (backward on the device, see ``_AttnFunction``).
+    """
+    head_dim = Q.shape[-1]
+    if scale is None:
+        scale = head_dim**-0.5
+    if torch.is_grad_enabled() and (Q.requires_grad or K.requires_grad or V.requires_grad):
+        out = _AttnFunction.apply(Q, K, V, mask_bsr, scale)
+    else:
+        out = _attn_forward(Q, K, V, mask_bsr, scale)
+    return out if Q.is_cuda else out.to(Q.device)
