@@ -212,6 +212,14 @@ TRNSPARSE_API int trnsparse_bsr_attention(int64_t heads, int64_t seq, int64_t he
                             const void* K, const void* V, void* O, int dtype, double scale,
                             void* stream);
 
+/* Tensor-core form of trnsparse_bsr_attention for bf16, block size 128,
+ * head_dim 64 or 128, seq a multiple of 128: tcgen05 S = Q K^T and O += P V
+ * with TMEM accumulators, in the reference's two-pass softmax form (row max
+ * and sum over all stored blocks first, then exp(s - max) / sum @ V). */
+TRNSPARSE_API int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t head_dim, const int* block_row_ptr,
+                               const int* block_col_idx, const void* Q, const void* K, const void* V,
+                               void* O, double scale, void* stream);
+
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an
  * allocator or pool callback, or hosts with a fixed up-front memory budget).

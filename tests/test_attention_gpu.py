@@ -87,3 +87,33 @@ def test_attention_backward_matches_dense_autograd():
     for a, r in ((Q.grad, Q2.grad), (K.grad, K2.grad), (V.grad, V2.grad)):
         torch.testing.assert_close(a, r, atol=1e-4, rtol=1e-4)
     assert c is not None
+
+
+@pytest.mark.parametrize("hd,heads,seq", [(128, 2, 1024), (64, 3, 768), (128, 1, 128)])
+def test_attention_tensor_core_vs_cuda_core_and_oracle(hd, heads, seq):
+    from trnsparse_b200.ops import _attn_forward
+
+    mask = w.sliding_window_mask(seq=seq, window=3, n_global=1)
+    Q, K, V = w.attention_inputs(heads=heads, seq=seq, hd=hd, seed=hd + seq)
+    Qd, Kd, Vd = Q.cuda(), K.cuda(), V.cuda()
+    tc = _attn_forward(Qd, Kd, Vd, mask, hd**-0.5)
+    cc = _attn_forward(Qd, Kd, Vd, mask, hd**-0.5, cuda_cores=True)
+    assert ts._lib.device_error() == 0
+    assert rel_fro(tc.float(), cc.float()) <= 2e-2
+    for h in range(heads):
+        ref = oracle.block_sparse_attention(Q[0, h].float(), K[0, h].float(), V[0, h].float(),
+                                            mask.block_row_ptrs, mask.block_col_indices, 128)
+        assert rel_fro(tc[0, h].float(), ref) <= 2e-2
+
+
+def test_attention_tensor_core_empty_block_row():
+    seq, hd = 384, 128
+    rp = torch.tensor([0, 1, 1, 3])  # block-row 1 empty
+    ci = torch.tensor([0, 0, 2])
+    m = _Mask(rp, ci, 128, seq)
+    Q, K, V = w.attention_inputs(heads=2, seq=seq, hd=hd, seed=9)
+    got = ts.block_sparse_attention_tiled(Q.cuda(), K.cuda(), V.cuda(), m).cpu()
+    assert torch.count_nonzero(got[0, :, 128:256]) == 0
+    for h in range(2):
+        ref = oracle.block_sparse_attention(Q[0, h].float(), K[0, h].float(), V[0, h].float(), rp, ci, 128)
+        assert rel_fro(got[0, h].float(), ref) <= 2e-2

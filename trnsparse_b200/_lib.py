@@ -53,6 +53,7 @@ SIGNATURES.update({
     "trnsparse_screened_spmm_workspace_size": [_i64, _i64],
     "trnsparse_screened_spmm": [_i64, _i64, _i64, _p, _i64, _p, _i32, _i64, _f64, _p, _i64, _p, _i64, _p, _sz, _p],
     "trnsparse_bsr_attention": [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32, _f64, _p],
+    "trnsparse_bsr_attention_tc": [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _f64, _p],
     "trnsparse_bsr_cg_noalloc": _BSR + [_p, _p, _i32, _p, _f64, _i32, _p, _p],
 })
 _RESTYPE = {

@@ -356,8 +356,12 @@ def screened_spmm(
 # ---------------------------------------------------------------------------
 
 
-def _attn_forward(Q, K, V, mask_bsr, scale):
-    """Device forward for (S, D) or (..., S, D) inputs sharing one mask."""
+def _attn_forward(Q, K, V, mask_bsr, scale, cuda_cores: bool = False):
+    """Device forward for (S, D) or (..., S, D) inputs sharing one mask.
+
+    bf16 with block size 128, head_dim 64/128 and seq a multiple of 128 runs
+    the tensor-core kernel; everything else (and ``cuda_cores=True``) runs
+    the CUDA-core kernel."""
     seq, hd = Q.shape[-2], Q.shape[-1]
     if Q.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"block_sparse_attention_tiled: dtype {Q.dtype} not supported (float32, bfloat16)")
@@ -375,7 +379,13 @@ def _attn_forward(Q, K, V, mask_bsr, scale):
     heads = Qd.numel() // (seq * hd) if seq * hd else 0
     O = torch.empty_like(Qd)
     code = _lib.F32 if Q.dtype == torch.float32 else _lib.BF16
+    tc = (not cuda_cores and Q.dtype == torch.bfloat16 and b == 128 and hd in (64, 128) and seq % 128 == 0
+          and heads > 0)
     with torch.cuda.device(dev):
+        if tc:
+            _lib.call("trnsparse_bsr_attention_tc", heads, seq, hd, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
+                      Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), float(scale), _lib.stream_handle(dev))
+            return O
         _lib.call("trnsparse_bsr_attention", heads, seq, hd, b, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
                   Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), code, float(scale), _lib.stream_handle(dev))
     return O
