@@ -350,6 +350,16 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
                                    "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / (tf32 / 3), 3),
                                    "peak": "tf32 derived / 3 passes"}
     del Ad, Qd, Bd
+    # config 4: block-sparse attention, 16 heads x 16384 x 128 bf16, sliding window 8 + 2 global
+    mask = w.sliding_window_mask()
+    Qa, Ka, Va = (t.cuda() for t in w.attention_inputs())
+    ms = time_call(lambda: ts.block_sparse_attention_tiled(Qa, Ka, Va, mask), 5, None)
+    fl = 4 * 128 ** 3 * mask.n_blocks * 16
+    ex["config4_block_sparse_attention_bf16"] = {
+        "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "blocks_per_head": mask.n_blocks,
+        "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 3), "peak": "bf16 measured",
+        "note": "FLOPs counted once per block (QK^T + PV); the kernel's two-pass softmax recomputes QK^T"}
+    del Qa, Ka, Va
     # config 5: Jacobi-PCG, 200 iterations, tol 0
     A5, b5 = w.block_pentadiagonal_spd()
     M5 = ts.jacobi_preconditioner_bsr(A5)
