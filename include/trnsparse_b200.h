@@ -220,6 +220,51 @@ TRNSPARSE_API int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t
                                const int* block_col_idx, const void* Q, const void* K, const void* V,
                                void* O, double scale, void* stream);
 
+/* ---- block-row-sharded CG (one process per GPU) --------------------------
+ * The multi-GPU form of cg_bsr (trnsparse/iterative.py:53-126; the
+ * reference itself has no multi-device code). A rank owns n_own rows; its
+ * BSR geometry has m = n_own rows and n = n_ext columns, columns >= n_own
+ * being halo copies of rows owned by other ranks. Workspace vectors are
+ * n_ext long (trnsparse_bsr_cg_workspace_size(n_ext, max_iter)); offsets[6]
+ * receives the byte offsets of {status, slots, r, p_even, p_odd, Ap}. Slot k
+ * (32 bytes) holds {p.Ap, r0.z0 (k = 0), r.r, r.z} for iteration k. Per
+ * iteration k the caller runs phase 0 (fused SpMV + p update), sums slot k's
+ * first double over ranks, runs phase 1 (x, r update), sums slot k's last two
+ * doubles over ranks and refreshes the halo part of r. dist_start needs the
+ * sum of status.bb and slot 0's second double over ranks before phase 0 of
+ * iteration 0. inv_d must hold the halo's inverse diagonal too. */
+TRNSPARSE_API int trnsparse_bsr_cg_layout(int64_t n, int max_iter, size_t* offsets);
+TRNSPARSE_API int trnsparse_bsr_cg_dist_start(int64_t n_own, int64_t n_ext, const float* b_vec, const float* inv_d,
+                                int max_iter, void* ws, size_t ws_bytes, void* stream);
+TRNSPARSE_API int trnsparse_bsr_cg_dist_phase(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                                double tol, int max_iter, int k, int phase, void* ws, void* stream);
+
+/* ---- peer memory for the sharded solvers (NVLink, one process per GPU) ---
+ * No reference counterpart (the reference has no multi-device code); used by
+ * the block-row-sharded CG instead of small NCCL collectives. peer_alloc
+ * returns a zeroed device buffer and its 64-byte CUDA IPC handle; other ranks
+ * open it with peer_open. peer_comm_bytes(world) is the size of the exchange
+ * area a buffer must reserve at `comm_off`. peer_reduce_push (one CTA):
+ * stores the halo rows listed in `sends` (int64 triples: source element
+ * offset in `src`, destination rank, destination byte offset in that rank's
+ * buffer; `chunk` floats each) and the local partials *my_a, *my_b into every
+ * peer, raises this rank's flag, waits (bounded) for all peers' flags for
+ * (epoch * stride + step + 1), then overwrites *my_a, *my_b with the sums
+ * over ranks in rank order. `peers` is a DEVICE array of `world` buffer
+ * addresses (this rank's own at index `rank`). Alternate `area` 0 / 1 between
+ * consecutive exchanges; call peer_bump_epoch once per solve on every rank. */
+TRNSPARSE_API size_t trnsparse_peer_comm_bytes(int world);
+TRNSPARSE_API int trnsparse_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+TRNSPARSE_API int trnsparse_peer_open(const void* ipc_handle, void** ptr);
+TRNSPARSE_API int trnsparse_peer_close(void* ptr);
+TRNSPARSE_API int trnsparse_peer_free(void* ptr);
+TRNSPARSE_API int trnsparse_peer_bump_epoch(void* mine, size_t comm_off, int world, void* stream);
+TRNSPARSE_API int trnsparse_peer_reduce_push(void* const* peers, int world, int rank, size_t comm_off, double* my_a,
+                               double* my_b, int area, long long stride, long long step,
+                               const float* src, const long long* sends, int n_sends, int chunk,
+                               void* stream);
+
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an
  * allocator or pool callback, or hosts with a fixed up-front memory budget).

@@ -54,6 +54,17 @@ SIGNATURES.update({
     "trnsparse_screened_spmm": [_i64, _i64, _i64, _p, _i64, _p, _i32, _i64, _f64, _p, _i64, _p, _i64, _p, _sz, _p],
     "trnsparse_bsr_attention": [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32, _f64, _p],
     "trnsparse_bsr_attention_tc": [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _f64, _p],
+    "trnsparse_bsr_cg_layout": [_i64, _i32, C.POINTER(C.c_size_t)],
+    "trnsparse_bsr_cg_dist_start": [_i64, _i64, _p, _p, _i32, _p, _sz, _p],
+    "trnsparse_bsr_cg_dist_phase": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p],
+    "trnsparse_peer_comm_bytes": [_i32],
+    "trnsparse_peer_alloc": [_sz, C.POINTER(C.c_void_p), _p],
+    "trnsparse_peer_open": [_p, C.POINTER(C.c_void_p)],
+    "trnsparse_peer_close": [_p],
+    "trnsparse_peer_free": [_p],
+    "trnsparse_peer_bump_epoch": [_p, _sz, _i32, _p],
+    "trnsparse_peer_reduce_push": [_p, _i32, _i32, _sz, _p, _p, _i32, C.c_longlong, C.c_longlong, _p, _p, _i32,
+                                   _i32, _p],
     "trnsparse_bsr_cg_noalloc": _BSR + [_p, _p, _i32, _p, _f64, _i32, _p, _p],
 })
 _RESTYPE = {
@@ -62,6 +73,7 @@ _RESTYPE = {
     "trnsparse_bsr_power_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_workspace_size": C.c_size_t,
     "trnsparse_screened_spmm_workspace_size": C.c_size_t,
+    "trnsparse_peer_comm_bytes": C.c_size_t,
 }
 
 _lib = None

@@ -30,7 +30,12 @@ struct SolverStatus {
 };
 static_assert(sizeof(SolverStatus) == 64, "status layout");
 
+// CG uses slot k as {a: p_k.Ap_k, b: r_0.z_0 (slot 0 only), c: r_{k+1}.r_{k+1},
+// d: r_{k+1}.z_{k+1}}; c and d are adjacent so a distributed solve can reduce
+// both with one collective. Power iteration uses {a: lambda, b: ||A v||^2}.
 struct Slot { double a, b, c, d; };
+
+__device__ __forceinline__ double cg_rz(const Slot* s, int k) { return k == 0 ? s[0].b : s[k - 1].d; }
 
 inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
@@ -122,7 +127,7 @@ struct CgStartVec {
   }
   __device__ void finish(double t0, double t1) const {
     atomicAdd(&w.st->bb, t0);
-    atomicAdd(&w.slots[0].c, t1);
+    atomicAdd(&w.slots[0].b, t1);
   }
 };
 
@@ -144,7 +149,7 @@ struct CgStartMv {
   }
   __device__ void finish(double t0, double t1) const {
     atomicAdd(&w.st->bb, t0);
-    atomicAdd(&w.slots[0].c, t1);
+    atomicAdd(&w.slots[0].b, t1);
   }
 };
 
@@ -158,6 +163,7 @@ struct CgMv {
   float* pcur;
   int k, max_iter;
   double tol;
+  int64_t halo_begin;  // columns >= halo_begin are halo copies of other ranks' rows (sharded solve)
   mutable float beta;
   __device__ bool begin(int cta) const {
     SolverStatus* st = w.st;
@@ -171,7 +177,7 @@ struct CgMv {
       beta = 0.f;
       return true;
     }
-    const double rel = (double)(float)sqrt(w.slots[k - 1].b) / bnorm;
+    const double rel = (double)(float)sqrt(w.slots[k - 1].c) / bnorm;
     if (rel < tol) {
       if (cta == 0 && threadIdx.x == 0) set_done(st, k, REASON_CONVERGED, rel);
       return false;
@@ -180,7 +186,7 @@ struct CgMv {
       if (cta == 0 && threadIdx.x == 0) set_done(st, max_iter, REASON_MAXITER, rel);
       return false;
     }
-    beta = (float)(w.slots[k].c / w.slots[k - 1].c);
+    beta = (float)(cg_rz(w.slots, k) / cg_rz(w.slots, k - 1));
     return true;
   }
   __device__ __forceinline__ float pk(int64_t c) const {
@@ -188,8 +194,18 @@ struct CgMv {
     const float z = inv_d ? __fmul_rn(r, inv_d[c]) : r;
     return __fadd_rn(z, __fmul_rn(beta, pprev[c]));
   }
-  __device__ float x(int64_t c) const { return pk(c); }
-  __device__ float4 x4(int64_t c) const { return make_float4(pk(c), pk(c + 1), pk(c + 2), pk(c + 3)); }
+  // Halo entries of p_k are stored by whichever thread computes them (every
+  // writer stores the same value), so the next iteration finds p_k there.
+  __device__ float x(int64_t c) const {
+    const float p = pk(c);
+    if (c >= halo_begin) pcur[c] = p;
+    return p;
+  }
+  __device__ float4 x4(int64_t c) const {
+    const float4 p = make_float4(pk(c), pk(c + 1), pk(c + 2), pk(c + 3));
+    if (c >= halo_begin) *reinterpret_cast<float4*>(pcur + c) = p;
+    return p;
+  }
   __device__ void row(int64_t i, float y, double* d0, double*) const {
     const float p = pk(i);
     pcur[i] = p;
@@ -214,12 +230,12 @@ struct CgUpdate {
     const double pap = w.slots[k].a;
     if (fabs(pap) < 1e-30) {
       if (cta == 0 && threadIdx.x == 0) {
-        const double rel = k > 0 ? (double)(float)sqrt(w.slots[k - 1].b) / sqrt(st->bb) : nan("");
+        const double rel = k > 0 ? (double)(float)sqrt(w.slots[k - 1].c) / sqrt(st->bb) : nan("");
         set_done(st, max_iter, REASON_BREAKDOWN, rel);
       }
       return false;
     }
-    alpha = (float)(w.slots[k].c / pap);
+    alpha = (float)(cg_rz(w.slots, k) / pap);
     return true;
   }
   __device__ void elem(int64_t i, double* d0, double* d1) const {
@@ -231,8 +247,8 @@ struct CgUpdate {
     *d1 += (double)r * (double)z;
   }
   __device__ void finish(double t0, double t1) const {
-    atomicAdd(&w.slots[k].b, t0);
-    atomicAdd(&w.slots[k + 1].c, t1);
+    atomicAdd(&w.slots[k].c, t0);
+    atomicAdd(&w.slots[k].d, t1);
   }
 };
 
@@ -460,7 +476,7 @@ extern "C" int trnsparse_bsr_cg_iterate(BSR_DESC_ARGS, float* x, const float* in
   for (int k = k_begin; k < k_end; ++k) {
     float* pcur = (k & 1) ? w.p1 : w.p0;
     const float* pprev = (k & 1) ? w.p0 : w.p1;
-    CgMv mv{inv_d, w, pprev, pcur, k, max_iter, tol, 0.f};
+    CgMv mv{inv_d, w, pprev, pcur, k, max_iter, tol, n, 0.f};
     rc = launch_bsr_mv(d, mv, vec_ok, st, "bsr_cg mv");
     if (rc) return rc;
     if (k >= max_iter) break;  // the launch above only records the final status
@@ -576,4 +592,56 @@ extern "C" int trnsparse_bsr_power_finish(int64_t n, float* v, int max_iter, voi
   if (n == 0) return TRNSPARSE_OK;
   const PowWs w = pow_ws(ws, n, max_iter);
   return launch_vec(n, PowFinal{w, v, 0.f, nullptr}, as_stream(stream), "bsr_power final");
+}
+
+// ---------------------------------------------------------------- sharded CG
+// A rank owns rows [0, n_own) of its block-rows; its BSR geometry has
+// m = n_own rows and n = n_ext columns, columns >= n_own being halo copies of
+// other ranks' rows. Vectors in the workspace are n_ext long. The caller
+// reduces the scalar slots across ranks between phases and refreshes the
+// halo part of r (and, once, inv_d) from the owning ranks.
+
+extern "C" int trnsparse_bsr_cg_layout(int64_t n, int max_iter, size_t* offsets) {
+  TSB_REQUIRE(offsets && n >= 0 && max_iter >= 0, "bsr_cg_layout: bad argument");
+  const size_t slots = align256(64);
+  const size_t vec0 = slots + align256(sizeof(Slot) * (size_t)(max_iter + 2));
+  const size_t vb = align256(sizeof(float) * (size_t)n);
+  offsets[0] = 0;           // status record
+  offsets[1] = slots;       // Slot[max_iter + 2], 32 bytes each
+  offsets[2] = vec0;        // r
+  offsets[3] = vec0 + vb;   // p (even k)
+  offsets[4] = vec0 + 2 * vb;  // p (odd k)
+  offsets[5] = vec0 + 3 * vb;  // Ap
+  return TRNSPARSE_OK;
+}
+
+extern "C" int trnsparse_bsr_cg_dist_start(int64_t n_own, int64_t n_ext, const float* b_vec, const float* inv_d,
+                                           int max_iter, void* ws, size_t ws_bytes, void* stream) {
+  TSB_REQUIRE(n_own >= 0 && n_ext >= n_own && max_iter >= 0 && b_vec && ws, "bsr_cg_dist_start: bad argument");
+  TSB_REQUIRE(ws_bytes >= cg_ws_size(n_ext, max_iter), "bsr_cg_dist_start: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  cudaError_t e = cudaMemsetAsync(ws, 0, cg_ws_size(n_ext, max_iter), st);  // scalars, r/p halos, p_{-1}
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_dist_start: memset");
+  if (n_own == 0) return TRNSPARSE_OK;
+  return launch_vec(n_own, CgStartVec{b_vec, inv_d, cg_ws(ws, n_ext, max_iter)}, st, "bsr_cg_dist_start");
+}
+
+extern "C" int trnsparse_bsr_cg_dist_phase(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                           const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                                           double tol, int max_iter, int k, int phase, void* ws, void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_cg_dist_phase");
+  if (rc) return rc;
+  TSB_REQUIRE(ws && x && k >= 0 && k <= max_iter && (phase == 0 || phase == 1), "bsr_cg_dist_phase: bad argument");
+  if (m == 0) return TRNSPARSE_OK;
+  cudaStream_t st = as_stream(stream);
+  const CgWs w = cg_ws(ws, n, max_iter);
+  float* pcur = (k & 1) ? w.p1 : w.p0;
+  const float* pprev = (k & 1) ? w.p0 : w.p1;
+  if (phase == 0) {
+    CgMv mv{inv_d, w, pprev, pcur, k, max_iter, tol, m, 0.f};
+    return launch_bsr_mv(d, mv, all_aligned({inv_d, w.r, w.p0, w.p1}), st, "bsr_cg_dist mv");
+  }
+  if (k >= max_iter) return TRNSPARSE_OK;
+  return launch_vec(m, CgUpdate{inv_d, x, w, pcur, k, max_iter, 0.f}, st, "bsr_cg_dist update");
 }
