@@ -265,6 +265,26 @@ TRNSPARSE_API int trnsparse_peer_reduce_push(void* const* peers, int world, int 
                                const float* src, const long long* sends, int n_sends, int chunk,
                                void* stream);
 
+/* Sharded CG with the exchanges fused into the solver kernels (no reference
+ * counterpart; multi-GPU form of iterative.py:53-126). Same workspace and
+ * iteration protocol as trnsparse_bsr_cg_dist_*, but the workspace must lie
+ * at offset 0 of this rank's trnsparse_peer_alloc buffer and no host-side
+ * reduction or halo exchange is needed: the last CTA of each kernel stores the
+ * rank's partial sums (and, after the x/r update, the halo rows of r listed in
+ * `sends`, `b` floats each) into every peer's buffer and raises a flag; the
+ * next kernel waits (bounded) for all flags and sums in rank order. Block size
+ * 128, block-aligned shapes. `peers` is a device array of the world's buffer
+ * addresses. Every rank must make the same sequence of calls. */
+TRNSPARSE_API int trnsparse_bsr_cg_fused_start(int64_t n_own, int64_t n_ext, int b, const float* b_vec,
+                                 const float* inv_d, int max_iter, void* ws, size_t ws_bytes,
+                                 void* const* peers, int world, int rank, size_t comm_off,
+                                 const long long* sends, int n_sends, void* stream);
+TRNSPARSE_API int trnsparse_bsr_cg_fused_phase(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                 const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                                 double tol, int max_iter, int k, int phase, void* ws, void* const* peers,
+                                 int world, int rank, size_t comm_off, const long long* sends, int n_sends,
+                                 void* stream);
+
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an
  * allocator or pool callback, or hosts with a fixed up-front memory budget).

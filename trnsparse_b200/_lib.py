@@ -65,6 +65,8 @@ SIGNATURES.update({
     "trnsparse_peer_bump_epoch": [_p, _sz, _i32, _p],
     "trnsparse_peer_reduce_push": [_p, _i32, _i32, _sz, _p, _p, _i32, C.c_longlong, C.c_longlong, _p, _p, _i32,
                                    _i32, _p],
+    "trnsparse_bsr_cg_fused_start": [_i64, _i64, _i32, _p, _p, _i32, _p, _sz, _p, _i32, _i32, _sz, _p, _i32, _p],
+    "trnsparse_bsr_cg_fused_phase": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_noalloc": _BSR + [_p, _p, _i32, _p, _f64, _i32, _p, _p],
 })
 _RESTYPE = {

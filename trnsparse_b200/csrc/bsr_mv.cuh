@@ -24,6 +24,8 @@
 //   void   finish(double d0, double d1)       CTA totals (thread 0 only)
 #pragma once
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace tsb {
@@ -42,48 +44,65 @@ __device__ __forceinline__ double block_sum256(double v, double* red /* [8] */) 
   return t;  // valid in thread 0
 }
 
+// Ops may define `void tail() const`, run by every thread of the CTA after
+// finish() (used by the sharded solver to publish results from the last CTA).
+template <class Op, class = void>
+struct HasTail { static constexpr bool value = false; };
+template <class Op>
+struct HasTail<Op, decltype(void(std::declval<const Op&>().tail()))> { static constexpr bool value = true; };
+
+template <class Op>
+__device__ __forceinline__ void run_tail(const Op& op) {
+  if constexpr (HasTail<Op>::value) op.tail();
+}
+
 template <class Op>
 __global__ void __launch_bounds__(256)
 bsr128_mv_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_idx,
-                 const float4* __restrict__ blocks, Op op) {
+                 const float4* __restrict__ blocks, int n_block_rows, Op op) {
   __shared__ float ys[128];
   __shared__ double red[8];
-  const int i = blockIdx.x;
-  if (!op.begin(i)) return;
+  if (!op.begin(blockIdx.x)) return;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float acc[16];
+  double d0 = 0.0, d1 = 0.0;
+  // one block-row per iteration; the grid may be smaller than the number of
+  // block-rows (persistent CTAs), so per-CTA prologue costs are paid once
+  for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x) {
+    float acc[16];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-  const int e = row_ptr[i + 1];
-  for (int idx = row_ptr[i]; idx < e; ++idx) {
-    const int64_t j = col_idx[idx];
-    const float4 xv = op.x4(j * 128 + 4 * lane);
-    const float4* bp = blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
-    float4 a[16];
+    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+    const int e = row_ptr[i + 1];
+    for (int idx = row_ptr[i]; idx < e; ++idx) {
+      const int64_t j = col_idx[idx];
+      const float4 xv = op.x4(j * 128 + 4 * lane);
+      const float4* bp = blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
+      float4 a[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) a[r] = __ldcs(bp + r * 32);
+      for (int r = 0; r < 16; ++r) a[r] = __ldcs(bp + r * 32);
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        acc[r] = fmaf(a[r].x, xv.x, acc[r]);
+        acc[r] = fmaf(a[r].y, xv.y, acc[r]);
+        acc[r] = fmaf(a[r].z, xv.z, acc[r]);
+        acc[r] = fmaf(a[r].w, xv.w, acc[r]);
+      }
+    }
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      acc[r] = fmaf(a[r].x, xv.x, acc[r]);
-      acc[r] = fmaf(a[r].y, xv.y, acc[r]);
-      acc[r] = fmaf(a[r].z, xv.z, acc[r]);
-      acc[r] = fmaf(a[r].w, xv.w, acc[r]);
+      const float v = warp_sum(acc[r]);
+      if (lane == r) ys[w * 16 + r] = v;
     }
+    __syncthreads();
+    if (threadIdx.x < 128) op.row(static_cast<int64_t>(i) * 128 + threadIdx.x, ys[threadIdx.x], &d0, &d1);
+    __syncthreads();
   }
-#pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    const float v = warp_sum(acc[r]);
-    if (lane == r) ys[w * 16 + r] = v;
-  }
-  __syncthreads();
-  double d0 = 0.0, d1 = 0.0;
-  if (threadIdx.x < 128) op.row(static_cast<int64_t>(i) * 128 + threadIdx.x, ys[threadIdx.x], &d0, &d1);
   if (Op::kDots > 0) {
     const double t0 = block_sum256(d0, red);
     double t1 = 0.0;
     if (Op::kDots > 1) t1 = block_sum256(d1, red);
     if (threadIdx.x == 0) op.finish(t0, t1);
   }
+  run_tail(op);
 }
 
 template <class Op>
@@ -115,6 +134,7 @@ bsr_generic_mv_kernel(int64_t m, int64_t n, int b, const int* __restrict__ row_p
     if (Op::kDots > 1) t1 = block_sum256(d1, red);
     if (threadIdx.x == 0) op.finish(t0, t1);
   }
+  run_tail(op);
 }
 
 // Geometry of a BSR operand as the kernels see it.
@@ -132,13 +152,16 @@ struct BsrDesc {
 };
 
 // Launches the right kernel for `d`; `vec_ok` says the Op's x4 may be used.
+// max_ctas > 0 caps the fast kernel's grid (persistent CTAs looping over block-rows).
 template <class Op>
-int launch_bsr_mv(const BsrDesc& d, const Op& op, bool vec_ok, cudaStream_t st, const char* what) {
+int launch_bsr_mv(const BsrDesc& d, const Op& op, bool vec_ok, cudaStream_t st, const char* what, int64_t max_ctas = 0) {
   if (d.fast() && vec_ok) {
-    const int64_t g = d.block_rows();
+    const int64_t nbr = d.block_rows();
+    int64_t g = nbr;
+    if (max_ctas > 0 && g > max_ctas) g = max_ctas;
     if (g > 0)
       bsr128_mv_kernel<Op><<<(unsigned)g, 256, 0, st>>>(d.row_ptr, d.col_idx,
-                                                       reinterpret_cast<const float4*>(d.blocks), op);
+                                                       reinterpret_cast<const float4*>(d.blocks), (int)nbr, op);
   } else {
     const int64_t g = (d.m + 255) / 256;
     if (g > 0) bsr_generic_mv_kernel<Op><<<(unsigned)g, 256, 0, st>>>(d.m, d.n, d.b, d.row_ptr, d.col_idx, d.blocks, op);

@@ -10,6 +10,7 @@
 // operation (separate roundings, scalars rounded to float32 where torch
 // would), except that inner products are accumulated in float64.
 #include "bsr_mv.cuh"
+#include "ptx.cuh"
 
 #include <math.h>
 
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(256) vec_kernel(int64_t n, Op op) {
   const double t0 = block_sum256(d0, red);
   const double t1 = block_sum256(d1, red);
   if (threadIdx.x == 0) op.finish(t0, t1);
+  run_tail(op);
 }
 
 inline unsigned vec_grid(int64_t n) {
@@ -411,8 +413,10 @@ bool all_aligned(std::initializer_list<const void*> ps) {
 }
 
 template <class Op>
-int launch_vec(int64_t n, const Op& op, cudaStream_t st, const char* what) {
-  vec_kernel<Op><<<vec_grid(n), 256, 0, st>>>(n, op);
+int launch_vec(int64_t n, const Op& op, cudaStream_t st, const char* what, unsigned max_ctas = 0) {
+  unsigned g = vec_grid(n);
+  if (max_ctas > 0 && g > max_ctas) g = max_ctas;
+  vec_kernel<Op><<<g, 256, 0, st>>>(n, op);
   TSB_CHECK_LAUNCH(what);
   return TRNSPARSE_OK;
 }
@@ -644,4 +648,306 @@ extern "C" int trnsparse_bsr_cg_dist_phase(int64_t m, int64_t n, int b, int64_t 
   }
   if (k >= max_iter) return TRNSPARSE_OK;
   return launch_vec(m, CgUpdate{inv_d, x, w, pcur, k, max_iter, 0.f}, st, "bsr_cg_dist update");
+}
+
+// ---------------------------------------------------------------- sharded CG, communication fused
+// Same iteration as the sharded phases above, but the exchanges happen inside
+// the solver kernels: the last CTA of a kernel (ticket counter) pushes this
+// rank's partial sums — and, after the x/r update, its boundary rows of r —
+// straight into every peer's buffer over NVLink and raises its flag; the next
+// kernel's CTAs wait (bounded) in their prologue for every peer's flag and
+// sum the partials in rank order. Two launches per iteration, no host
+// involvement. The buffers are the CUDA-IPC mapped ones of trnsparse_peer_*;
+// the exchange area layout is the one documented in peer.cu, with three
+// ticket counters after the epoch.
+namespace tsb {
+namespace {
+
+struct PeerCtx {
+  char* const* peers;   // device array, world entries
+  int world, rank;
+  size_t comm_off;
+  long long stride;
+  const long long* sends;  // halo r rows: (src elem offset, dst rank, dst byte offset)
+  int n_sends, chunk;
+};
+
+__device__ __forceinline__ long long* pc_flags(const PeerCtx& p, char* base) {
+  return reinterpret_cast<long long*>(base + p.comm_off);
+}
+__device__ __forceinline__ double* pc_vals(const PeerCtx& p, char* base) {
+  return reinterpret_cast<double*>(base + p.comm_off + 16 * p.world);
+}
+__device__ __forceinline__ long long* pc_epoch(const PeerCtx& p, char* base) {
+  return reinterpret_cast<long long*>(base + p.comm_off + 48 * p.world);
+}
+__device__ __forceinline__ unsigned int* pc_ticket(const PeerCtx& p, int which) {
+  return reinterpret_cast<unsigned int*>(p.peers[p.rank] + p.comm_off + 48 * p.world + 8) + which;
+}
+__device__ __forceinline__ long long pc_seq(const PeerCtx& p, long long step) {
+  return (*reinterpret_cast<volatile long long*>(pc_epoch(p, p.peers[p.rank]))) * p.stride + step + 1;
+}
+
+__device__ __forceinline__ long long ld_acq_sys(const long long* q) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];\n" : "=l"(v) : "l"(q) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_rel_sys(long long* q, long long v) {
+  asm volatile("st.release.sys.global.s64 [%0], %1;\n" ::"l"(q), "l"(v) : "memory");
+}
+
+// All threads of the CTA: wait for every rank's flag of `area` to reach the
+// step's sequence number, then return the rank-ordered sums of its partials.
+__device__ double2 pc_wait_sum(const PeerCtx& p, int area, long long step) {
+  __shared__ double2 tot;
+  char* mine = p.peers[p.rank];
+  const long long seq = pc_seq(p, step);
+  if (threadIdx.x < p.world) {
+    const long long* f = pc_flags(p, mine) + area * p.world + threadIdx.x;
+    uint32_t i = 0;
+    while (ld_acq_sys(f) < seq) {
+      if (++i > kSpinLimit) {
+        record_device_error(DEVERR_PEER_TIMEOUT);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const volatile double* v = pc_vals(p, mine) + area * p.world * 2;
+    double a = 0.0, b = 0.0;
+    for (int q = 0; q < p.world; ++q) {
+      a += v[2 * q];
+      b += v[2 * q + 1];
+    }
+    tot = make_double2(a, b);
+  }
+  __syncthreads();
+  return tot;
+}
+
+// All threads: if this is the kernel's last CTA, publish the complete local
+// partials (*a, *b) and optionally the halo rows of `src`, then raise flags.
+__device__ void pc_publish(const PeerCtx& p, int which, int area, long long step, const double* a, const double* b,
+                           const float* src, bool halo) {
+  __shared__ int last;
+  __shared__ double2 part;
+  __syncthreads();  // every thread's stores of this CTA precede the ticket
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(pc_ticket(p, which), 1u);
+    last = ((t + 1) % gridDim.x) == 0;
+    if (last) {
+      __threadfence();
+      part = make_double2(a ? *(volatile const double*)a : 0.0, b ? *(volatile const double*)b : 0.0);
+    }
+  }
+  __syncthreads();
+  if (!last) return;
+  const long long seq = pc_seq(p, step);
+  if (halo) {
+    for (int s = 0; s < p.n_sends; ++s) {
+      const long long so = p.sends[3 * s], dr = p.sends[3 * s + 1], dofs = p.sends[3 * s + 2];
+      float4* dst = reinterpret_cast<float4*>(p.peers[dr] + dofs);
+      const volatile float4* sp = reinterpret_cast<const volatile float4*>(src + so);
+      for (int i = threadIdx.x; i < p.chunk / 4; i += blockDim.x) {
+        const float4 v = make_float4(sp[i].x, sp[i].y, sp[i].z, sp[i].w);
+        dst[i] = v;
+      }
+    }
+  }
+  if (threadIdx.x < p.world) {
+    double* v = pc_vals(p, p.peers[threadIdx.x]) + (area * p.world + p.rank) * 2;
+    v[0] = part.x;
+    v[1] = part.y;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world) st_rel_sys(pc_flags(p, p.peers[threadIdx.x]) + area * p.world + p.rank, seq);
+}
+
+// step numbering: 0 = setup, 1 + 2k = p.Ap of iteration k, 2 + 2k = r.r / r.z of iteration k
+
+struct CgStartFused {
+  const float *b, *inv_d;
+  CgWs w;
+  PeerCtx p;
+  __device__ bool begin(int) const { return true; }
+  __device__ void elem(int64_t i, double* d0, double* d1) const {
+    const float r = b[i];
+    w.r[i] = r;
+    const float z = inv_d ? __fmul_rn(r, inv_d[i]) : r;
+    *d0 += (double)b[i] * (double)b[i];
+    *d1 += (double)r * (double)z;
+  }
+  __device__ void finish(double t0, double t1) const {
+    atomicAdd(&w.st->bb, t0);
+    atomicAdd(&w.slots[0].b, t1);
+  }
+  __device__ void tail() const { pc_publish(p, 0, 1, 0, &w.st->bb, &w.slots[0].b, w.r, true); }
+};
+
+struct CgMvFused {
+  static constexpr int kDots = 1;
+  const float* inv_d;
+  CgWs w;
+  const float* pprev;
+  float* pcur;
+  int k, max_iter;
+  double tol;
+  int64_t halo_begin;
+  PeerCtx p;
+  mutable float beta;
+  __device__ bool begin(int cta) const {
+    SolverStatus* st = w.st;
+    if (*(volatile int*)&st->done) return false;
+    const double2 t = pc_wait_sum(p, 1, k == 0 ? 0 : 2 + 2 * (k - 1));
+    if (k == 0) {
+      const double bnorm = sqrt(t.x);
+      if (cta == 0 && threadIdx.x == 0) {
+        st->bb = t.x;
+        w.slots[0].b = t.y;
+      }
+      if (bnorm < 1e-15) {
+        if (cta == 0 && threadIdx.x == 0) set_done(st, 0, REASON_ZERO_RHS, 0.0);
+        return false;
+      }
+      beta = 0.f;
+      return true;
+    }
+    if (cta == 0 && threadIdx.x == 0) {
+      w.slots[k - 1].c = t.x;
+      w.slots[k - 1].d = t.y;
+    }
+    const double bnorm = sqrt(*(volatile double*)&st->bb);
+    const double rel = (double)(float)sqrt(t.x) / bnorm;
+    if (rel < tol) {
+      if (cta == 0 && threadIdx.x == 0) set_done(st, k, REASON_CONVERGED, rel);
+      return false;
+    }
+    if (k >= max_iter) {
+      if (cta == 0 && threadIdx.x == 0) set_done(st, max_iter, REASON_MAXITER, rel);
+      return false;
+    }
+    const double rz_prev = k == 1 ? *(volatile double*)&w.slots[0].b : *(volatile double*)&w.slots[k - 2].d;
+    beta = (float)(t.y / rz_prev);
+    return true;
+  }
+  __device__ __forceinline__ float pk(int64_t c) const {
+    const float r = w.r[c];
+    const float z = inv_d ? __fmul_rn(r, inv_d[c]) : r;
+    return __fadd_rn(z, __fmul_rn(beta, pprev[c]));
+  }
+  __device__ float x(int64_t c) const {
+    const float v = pk(c);
+    if (c >= halo_begin) pcur[c] = v;
+    return v;
+  }
+  __device__ float4 x4(int64_t c) const {
+    const float4 v = make_float4(pk(c), pk(c + 1), pk(c + 2), pk(c + 3));
+    if (c >= halo_begin) *reinterpret_cast<float4*>(pcur + c) = v;
+    return v;
+  }
+  __device__ void row(int64_t i, float y, double* d0, double*) const {
+    const float v = pk(i);
+    pcur[i] = v;
+    w.ap[i] = y;
+    *d0 += (double)v * (double)y;
+  }
+  __device__ void finish(double t0, double) const { atomicAdd(&w.slots[k].a, t0); }
+  __device__ void tail() const { pc_publish(p, 1, 0, 1 + 2 * k, &w.slots[k].a, nullptr, nullptr, false); }
+};
+
+struct CgUpdateFused {
+  const float* inv_d;
+  float* x;
+  CgWs w;
+  const float* pcur;
+  int k, max_iter;
+  PeerCtx p;
+  mutable float alpha;
+  __device__ bool begin(int cta) const {
+    SolverStatus* st = w.st;
+    if (*(volatile int*)&st->done) return false;
+    const double2 t = pc_wait_sum(p, 0, 1 + 2 * k);
+    const double pap = t.x;
+    if (cta == 0 && threadIdx.x == 0) w.slots[k].a = pap;
+    if (fabs(pap) < 1e-30) {
+      if (cta == 0 && threadIdx.x == 0) {
+        const double rel = k > 0 ? (double)(float)sqrt(*(volatile double*)&w.slots[k - 1].c) /
+                                       sqrt(*(volatile double*)&st->bb)
+                                 : nan("");
+        set_done(st, max_iter, REASON_BREAKDOWN, rel);
+      }
+      return false;
+    }
+    const double rz = k == 0 ? *(volatile double*)&w.slots[0].b : *(volatile double*)&w.slots[k - 1].d;
+    alpha = (float)(rz / pap);
+    return true;
+  }
+  __device__ void elem(int64_t i, double* d0, double* d1) const {
+    x[i] = __fadd_rn(x[i], __fmul_rn(alpha, pcur[i]));
+    const float r = __fsub_rn(w.r[i], __fmul_rn(alpha, w.ap[i]));
+    w.r[i] = r;
+    const float z = inv_d ? __fmul_rn(r, inv_d[i]) : r;
+    *d0 += (double)r * (double)r;
+    *d1 += (double)r * (double)z;
+  }
+  __device__ void finish(double t0, double t1) const {
+    atomicAdd(&w.slots[k].c, t0);
+    atomicAdd(&w.slots[k].d, t1);
+  }
+  __device__ void tail() const { pc_publish(p, 2, 1, 2 + 2 * k, &w.slots[k].c, &w.slots[k].d, w.r, true); }
+};
+
+__global__ void fused_bump_epoch(char* const* peers, int rank, size_t comm_off, int world) {
+  *reinterpret_cast<long long*>(peers[rank] + comm_off + 48 * world) += 1;
+}
+
+}  // namespace
+}  // namespace tsb
+
+#define PEER_ARGS void* const* peers, int world, int rank, size_t comm_off, const long long* sends, int n_sends
+#define PEER_CTX PeerCtx{reinterpret_cast<char* const*>(peers), world, rank, comm_off, 2ll * max_iter + 4, sends, n_sends, b}
+
+extern "C" int trnsparse_bsr_cg_fused_start(int64_t n_own, int64_t n_ext, int b, const float* b_vec,
+                                            const float* inv_d, int max_iter, void* ws, size_t ws_bytes, PEER_ARGS,
+                                            void* stream) {
+  TSB_REQUIRE(n_own >= 0 && n_ext >= n_own && max_iter >= 0 && b_vec && ws && peers && world > 0 && rank >= 0 &&
+                  rank < world && (n_sends == 0 || sends),
+              "bsr_cg_fused_start: bad argument");
+  TSB_REQUIRE(ws_bytes >= cg_ws_size(n_ext, max_iter), "bsr_cg_fused_start: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  cudaError_t e = cudaMemsetAsync(ws, 0, cg_ws_size(n_ext, max_iter), st);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_fused_start: memset");
+  fused_bump_epoch<<<1, 1, 0, st>>>(reinterpret_cast<char* const*>(peers), rank, comm_off, world);
+  TSB_CHECK_LAUNCH("bsr_cg_fused_start: epoch");
+  return launch_vec(n_own, CgStartFused{b_vec, inv_d, cg_ws(ws, n_ext, max_iter), PEER_CTX}, st,
+                    "bsr_cg_fused_start");
+}
+
+extern "C" int trnsparse_bsr_cg_fused_phase(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                            const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                                            double tol, int max_iter, int k, int phase, void* ws, PEER_ARGS,
+                                            void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_cg_fused_phase");
+  if (rc) return rc;
+  TSB_REQUIRE(ws && x && k >= 0 && k <= max_iter && (phase == 0 || phase == 1) && peers && world > 0,
+              "bsr_cg_fused_phase: bad argument");
+  TSB_REQUIRE(d.fast(), "bsr_cg_fused_phase: needs block size 128 and block-aligned shapes");
+  cudaStream_t st = as_stream(stream);
+  const CgWs w = cg_ws(ws, n, max_iter);
+  float* pcur = (k & 1) ? w.p1 : w.p0;
+  const float* pprev = (k & 1) ? w.p0 : w.p1;
+  if (phase == 0) {
+    CgMvFused mv{inv_d, w, pprev, pcur, k, max_iter, tol, m, PEER_CTX, 0.f};
+    // persistent CTAs: every CTA pays the peer-flag wait of its prologue once
+    return launch_bsr_mv(d, mv, all_aligned({inv_d, w.r, w.p0, w.p1}), st, "bsr_cg_fused mv", 3 * sm_count());
+  }
+  if (k >= max_iter) return TRNSPARSE_OK;
+  return launch_vec(m, CgUpdateFused{inv_d, x, w, pcur, k, max_iter, PEER_CTX, 0.f}, st, "bsr_cg_fused update",
+                    sm_count());
 }

@@ -154,7 +154,9 @@ class ShardedCG:
     iteration budget.
 
     transport="nccl": scalar all-reduces and halo exchanges are NCCL
-    collectives / send-recv. transport="peer": the workspace lives in a CUDA
+    collectives / send-recv. transport="fused": the exchanges happen inside
+    the two solver kernels of an iteration (see trnsparse_bsr_cg_fused_*).
+    transport="peer": the workspace lives in a CUDA
     IPC buffer every rank maps, and one single-CTA kernel per exchange pushes
     the halo rows and partial sums straight into the peers' memory over
     NVLink, raises a flag and waits for the peers' flags (bounded), replacing
@@ -194,17 +196,17 @@ class ShardedCG:
         self.ws_bytes = _lib.raw("trnsparse_bsr_cg_workspace_size")(n_ext, max_iter)
         self.transport = transport
         self._peer_ptrs: list[int] = []
-        if transport == "peer":
+        if transport in ("peer", "fused"):
             self._setup_peer(max_iter)
         elif transport == "nccl":
             self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
         else:
-            raise ValueError(f"transport must be 'nccl' or 'peer', got {transport!r}")
+            raise ValueError(f"transport must be 'nccl', 'peer' or 'fused', got {transport!r}")
         offs = (ctypes.c_size_t * 6)()
         _lib.call("trnsparse_bsr_cg_layout", n_ext, max_iter, offs)
         self.offs = list(offs)
         self.r_vec = self.ws[offs[2] : offs[2] + 4 * n_ext].view(torch.float32)
-        if transport == "peer":
+        if transport in ("peer", "fused"):
             self._build_sends()
         self.graph = None
         if graph:
@@ -279,7 +281,7 @@ class ShardedCG:
 
     def close(self) -> None:
         """Release the peer mappings and the shared buffer (peer transport)."""
-        if self.transport != "peer" or not hasattr(self, "_own_ptr"):
+        if self.transport not in ("peer", "fused") or not hasattr(self, "_own_ptr"):
             return
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
@@ -295,6 +297,8 @@ class ShardedCG:
     def _solve(self, check: bool) -> None:
         if self.transport == "peer":
             return self._solve_peer()
+        if self.transport == "fused":
+            return self._solve_fused()
         lib, sh, ws, offs, g = self._lib, self.shard, self.ws, self.offs, self.group
         s = lib.stream_handle(self.dev)
         n_own, n_ext = sh.n_own, sh.n_ext
@@ -337,6 +341,23 @@ class ShardedCG:
             lib.call("trnsparse_bsr_cg_dist_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 1,
                      ws.data_ptr(), s)
             self._push(slot + 32 * k + 16, slot + 32 * k + 24, 1, 2 + 2 * k, True)  # r.r, r.z, halo of r
+
+    def _solve_fused(self) -> None:
+        lib, sh, ws = self._lib, self.shard, self.ws
+        s = lib.stream_handle(self.dev)
+        inv = lib.ptr(self.inv_d)
+        peer = (self.peers_dev.data_ptr(), self.world, self.rank, self.comm_off, self.sends_dev.data_ptr(),
+                self.n_sends)
+        self.x.zero_()
+        lib.call("trnsparse_bsr_cg_fused_start", sh.n_own, sh.n_ext, sh.block_size, self.b.data_ptr(), inv,
+                 self.max_iter, ws.data_ptr(), self.ws_bytes, *peer, s)
+        for k in range(self.max_iter + 1):
+            lib.call("trnsparse_bsr_cg_fused_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 0,
+                     ws.data_ptr(), *peer, s)
+            if k == self.max_iter:
+                break
+            lib.call("trnsparse_bsr_cg_fused_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 1,
+                     ws.data_ptr(), *peer, s)
 
     def run(self) -> tuple[torch.Tensor, int, float]:
         with torch.cuda.device(self.dev):
