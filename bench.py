@@ -294,7 +294,7 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict) -> dict:
     bl = b[sh.r0 * 128 : sh.r1 * 128].cuda()
     iters = 30
     out = {}
-    for transport in ("fused", "peer", "nccl"):
+    for transport in ("coop", "fused", "peer", "nccl"):
         cg = D.ShardedCG(sh, bl, tol=0.0, max_iter=iters, graph=True, transport=transport)
         cg.run()
         torch.cuda.synchronize()

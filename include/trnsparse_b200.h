@@ -252,8 +252,10 @@ TRNSPARSE_API int trnsparse_bsr_cg_dist_phase(int64_t m, int64_t n, int b, int64
  * peer, raises this rank's flag, waits (bounded) for all peers' flags for
  * (epoch * stride + step + 1), then overwrites *my_a, *my_b with the sums
  * over ranks in rank order. `peers` is a DEVICE array of `world` buffer
- * addresses (this rank's own at index `rank`). Alternate `area` 0 / 1 between
- * consecutive exchanges; call peer_bump_epoch once per solve on every rank. */
+ * addresses (this rank's own at index `rank`). area is 0, 1 or 2; two
+ * consecutive exchanges must use different areas (the sharded CG uses 2 for
+ * its setup exchange and alternates 0 / 1 per iteration); call
+ * peer_bump_epoch once per solve on every rank. */
 TRNSPARSE_API size_t trnsparse_peer_comm_bytes(int world);
 TRNSPARSE_API int trnsparse_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
 TRNSPARSE_API int trnsparse_peer_open(const void* ipc_handle, void** ptr);
@@ -284,6 +286,15 @@ TRNSPARSE_API int trnsparse_bsr_cg_fused_phase(int64_t m, int64_t n, int b, int6
                                  double tol, int max_iter, int k, int phase, void* ws, void* const* peers,
                                  int world, int rank, size_t comm_off, const long long* sends, int n_sends,
                                  void* stream);
+
+/* One cooperative launch per iteration of the fused sharded CG: the two
+ * phases of trnsparse_bsr_cg_fused_phase merged (iteration k; k == max_iter
+ * only records the final status). Same buffers, protocol and requirements as
+ * trnsparse_bsr_cg_fused_*; start with trnsparse_bsr_cg_fused_start. */
+TRNSPARSE_API int trnsparse_bsr_cg_coop_iter(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                               const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                               double tol, int max_iter, int k, void* ws, void* const* peers, int world,
+                               int rank, size_t comm_off, const long long* sends, int n_sends, void* stream);
 
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an

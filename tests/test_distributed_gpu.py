@@ -54,7 +54,7 @@ def _worker(rank, world, port, cases, out, transport="nccl"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["nccl", "peer", "fused"])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "fused", "coop"])
 def test_sharded_cg_two_gpus(transport):
     cases = [(64, 0.0, 30), (96, 1e-6, 100)] if transport == "nccl" else [(64, 0.0, 30), (96, 0.0, 40)]
     ctx = mp.get_context("spawn")

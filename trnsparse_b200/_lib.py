@@ -67,6 +67,7 @@ SIGNATURES.update({
                                    _i32, _p],
     "trnsparse_bsr_cg_fused_start": [_i64, _i64, _i32, _p, _p, _i32, _p, _sz, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_fused_phase": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
+    "trnsparse_bsr_cg_coop_iter": _BSR + [_p, _p, _f64, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_noalloc": _BSR + [_p, _p, _i32, _p, _f64, _i32, _p, _p],
 })
 _RESTYPE = {

@@ -598,6 +598,18 @@ extern "C" int trnsparse_bsr_power_finish(int64_t n, float* v, int max_iter, voi
   return launch_vec(n, PowFinal{w, v, 0.f, nullptr}, as_stream(stream), "bsr_power final");
 }
 
+// Clears the status record, the scalar slots and the p / Ap vectors of a CG
+// workspace, but not r: in a sharded solve a faster peer may already have
+// stored this solve's halo rows of r before this rank starts (the own part of
+// r is written by the start kernel).
+inline cudaError_t clear_cg_ws(void* ws, int64_t n_ext, int max_iter, cudaStream_t st) {
+  const size_t head = align256(64) + align256(sizeof(Slot) * (size_t)(max_iter + 2));
+  const size_t vb = align256(sizeof(float) * (size_t)n_ext);
+  cudaError_t e = cudaMemsetAsync(ws, 0, head, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(static_cast<char*>(ws) + head + vb, 0, 3 * vb, st);
+  return e;
+}
+
 // ---------------------------------------------------------------- sharded CG
 // A rank owns rows [0, n_own) of its block-rows; its BSR geometry has
 // m = n_own rows and n = n_ext columns, columns >= n_own being halo copies of
@@ -624,7 +636,7 @@ extern "C" int trnsparse_bsr_cg_dist_start(int64_t n_own, int64_t n_ext, const f
   TSB_REQUIRE(n_own >= 0 && n_ext >= n_own && max_iter >= 0 && b_vec && ws, "bsr_cg_dist_start: bad argument");
   TSB_REQUIRE(ws_bytes >= cg_ws_size(n_ext, max_iter), "bsr_cg_dist_start: workspace too small");
   cudaStream_t st = as_stream(stream);
-  cudaError_t e = cudaMemsetAsync(ws, 0, cg_ws_size(n_ext, max_iter), st);  // scalars, r/p halos, p_{-1}
+  cudaError_t e = clear_cg_ws(ws, n_ext, max_iter, st);
   if (e != cudaSuccess) return cuda_status(e, "bsr_cg_dist_start: memset");
   if (n_own == 0) return TRNSPARSE_OK;
   return launch_vec(n_own, CgStartVec{b_vec, inv_d, cg_ws(ws, n_ext, max_iter)}, st, "bsr_cg_dist_start");
@@ -676,13 +688,13 @@ __device__ __forceinline__ long long* pc_flags(const PeerCtx& p, char* base) {
   return reinterpret_cast<long long*>(base + p.comm_off);
 }
 __device__ __forceinline__ double* pc_vals(const PeerCtx& p, char* base) {
-  return reinterpret_cast<double*>(base + p.comm_off + 16 * p.world);
+  return reinterpret_cast<double*>(base + p.comm_off + 24 * p.world);
 }
 __device__ __forceinline__ long long* pc_epoch(const PeerCtx& p, char* base) {
-  return reinterpret_cast<long long*>(base + p.comm_off + 48 * p.world);
+  return reinterpret_cast<long long*>(base + p.comm_off + 72 * p.world);
 }
 __device__ __forceinline__ unsigned int* pc_ticket(const PeerCtx& p, int which) {
-  return reinterpret_cast<unsigned int*>(p.peers[p.rank] + p.comm_off + 48 * p.world + 8) + which;
+  return reinterpret_cast<unsigned int*>(p.peers[p.rank] + p.comm_off + 72 * p.world + 8) + which;
 }
 __device__ __forceinline__ long long pc_seq(const PeerCtx& p, long long step) {
   return (*reinterpret_cast<volatile long long*>(pc_epoch(p, p.peers[p.rank]))) * p.stride + step + 1;
@@ -786,7 +798,7 @@ struct CgStartFused {
     atomicAdd(&w.st->bb, t0);
     atomicAdd(&w.slots[0].b, t1);
   }
-  __device__ void tail() const { pc_publish(p, 0, 1, 0, &w.st->bb, &w.slots[0].b, w.r, true); }
+  __device__ void tail() const { pc_publish(p, 0, 2, 0, &w.st->bb, &w.slots[0].b, w.r, true); }
 };
 
 struct CgMvFused {
@@ -803,7 +815,7 @@ struct CgMvFused {
   __device__ bool begin(int cta) const {
     SolverStatus* st = w.st;
     if (*(volatile int*)&st->done) return false;
-    const double2 t = pc_wait_sum(p, 1, k == 0 ? 0 : 2 + 2 * (k - 1));
+    const double2 t = k == 0 ? pc_wait_sum(p, 2, 0) : pc_wait_sum(p, 1, 2 + 2 * (k - 1));
     if (k == 0) {
       const double bnorm = sqrt(t.x);
       if (cta == 0 && threadIdx.x == 0) {
@@ -903,7 +915,7 @@ struct CgUpdateFused {
 };
 
 __global__ void fused_bump_epoch(char* const* peers, int rank, size_t comm_off, int world) {
-  *reinterpret_cast<long long*>(peers[rank] + comm_off + 48 * world) += 1;
+  *reinterpret_cast<long long*>(peers[rank] + comm_off + 72 * world) += 1;
 }
 
 }  // namespace
@@ -920,7 +932,7 @@ extern "C" int trnsparse_bsr_cg_fused_start(int64_t n_own, int64_t n_ext, int b,
               "bsr_cg_fused_start: bad argument");
   TSB_REQUIRE(ws_bytes >= cg_ws_size(n_ext, max_iter), "bsr_cg_fused_start: workspace too small");
   cudaStream_t st = as_stream(stream);
-  cudaError_t e = cudaMemsetAsync(ws, 0, cg_ws_size(n_ext, max_iter), st);
+  cudaError_t e = clear_cg_ws(ws, n_ext, max_iter, st);
   if (e != cudaSuccess) return cuda_status(e, "bsr_cg_fused_start: memset");
   fused_bump_epoch<<<1, 1, 0, st>>>(reinterpret_cast<char* const*>(peers), rank, comm_off, world);
   TSB_CHECK_LAUNCH("bsr_cg_fused_start: epoch");
@@ -950,4 +962,99 @@ extern "C" int trnsparse_bsr_cg_fused_phase(int64_t m, int64_t n, int b, int64_t
   if (k >= max_iter) return TRNSPARSE_OK;
   return launch_vec(m, CgUpdateFused{inv_d, x, w, pcur, k, max_iter, PEER_CTX, 0.f}, st, "bsr_cg_fused update",
                     sm_count());
+}
+
+// ---------------------------------------------------------------- sharded CG, one kernel per iteration
+// The two fused kernels of an iteration merged into one cooperative launch
+// (all CTAs co-resident): prologue waits for the previous iteration's
+// r.r / r.z and halo, SpMV with p on the fly, last CTA publishes p.Ap, every
+// CTA waits for the global p.Ap, updates x and r on the rows it computed and
+// the last CTA publishes r.r / r.z and the halo rows of r.
+namespace tsb {
+namespace {
+
+__global__ void __launch_bounds__(256)
+cg_iter_coop_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_idx,
+                    const float4* __restrict__ blocks, int n_block_rows, CgMvFused mv, CgUpdateFused up) {
+  __shared__ float ys[128];
+  __shared__ double red[8];
+  if (!mv.begin(blockIdx.x)) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  double d0 = 0.0, d1 = 0.0;
+  for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x) {
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+    const int e = row_ptr[i + 1];
+    for (int idx = row_ptr[i]; idx < e; ++idx) {
+      const int64_t j = col_idx[idx];
+      const float4 xv = mv.x4(j * 128 + 4 * lane);
+      const float4* bp = blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
+      float4 a[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) a[r] = __ldcs(bp + r * 32);
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        acc[r] = fmaf(a[r].x, xv.x, acc[r]);
+        acc[r] = fmaf(a[r].y, xv.y, acc[r]);
+        acc[r] = fmaf(a[r].z, xv.z, acc[r]);
+        acc[r] = fmaf(a[r].w, xv.w, acc[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float v = warp_sum(acc[r]);
+      if (lane == r) ys[w * 16 + r] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 128) mv.row(static_cast<int64_t>(i) * 128 + threadIdx.x, ys[threadIdx.x], &d0, &d1);
+    __syncthreads();
+  }
+  {
+    const double t0 = block_sum256(d0, red);
+    if (threadIdx.x == 0) mv.finish(t0, 0.0);
+  }
+  mv.tail();
+  if (mv.k >= mv.max_iter) return;
+  if (!up.begin(blockIdx.x)) return;
+  double e0 = 0.0, e1 = 0.0;
+  for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x)
+    if (threadIdx.x < 128) up.elem(static_cast<int64_t>(i) * 128 + threadIdx.x, &e0, &e1);
+  const double t0 = block_sum256(e0, red);
+  const double t1 = block_sum256(e1, red);
+  if (threadIdx.x == 0) up.finish(t0, t1);
+  up.tail();
+}
+
+}  // namespace
+}  // namespace tsb
+
+extern "C" int trnsparse_bsr_cg_coop_iter(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                          const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                                          double tol, int max_iter, int k, void* ws, PEER_ARGS, void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_cg_coop_iter");
+  if (rc) return rc;
+  TSB_REQUIRE(ws && x && k >= 0 && k <= max_iter && peers && world > 0, "bsr_cg_coop_iter: bad argument");
+  TSB_REQUIRE(d.fast(), "bsr_cg_coop_iter: needs block size 128 and block-aligned shapes");
+  cudaStream_t st = as_stream(stream);
+  const CgWs w = cg_ws(ws, n, max_iter);
+  TSB_REQUIRE(all_aligned({inv_d, w.r, w.p0, w.p1, x}), "bsr_cg_coop_iter: vectors must be 16-byte aligned");
+  float* pcur = (k & 1) ? w.p1 : w.p0;
+  const float* pprev = (k & 1) ? w.p0 : w.p1;
+  CgMvFused mv{inv_d, w, pprev, pcur, k, max_iter, tol, m, PEER_CTX, 0.f};
+  CgUpdateFused up{inv_d, x, w, pcur, k, max_iter, PEER_CTX, 0.f};
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cg_iter_coop_kernel, 256, 0);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_coop_iter: occupancy");
+  int64_t nbr = d.block_rows();
+  int64_t grid = static_cast<int64_t>(sm_count()) * (per_sm < 1 ? 1 : per_sm);
+  if (grid > nbr) grid = nbr;
+  if (grid < 1) grid = 1;
+  const float4* bl = reinterpret_cast<const float4*>(blocks);
+  int nbr_i = (int)nbr;
+  void* args[] = {(void*)&row_ptr, (void*)&col_idx, (void*)&bl, (void*)&nbr_i, (void*)&mv, (void*)&up};
+  e = cudaLaunchCooperativeKernel((const void*)cg_iter_coop_kernel, dim3((unsigned)grid), dim3(256), args, 0, st);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_coop_iter: cooperative launch");
+  return TRNSPARSE_OK;
 }

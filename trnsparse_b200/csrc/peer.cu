@@ -6,15 +6,18 @@
 // store straight into a peer's memory over NVLink. The buffer holds the
 // rank's solver workspace (so halo rows are written directly into the
 // receiver's vectors) followed by a small exchange area:
-//   flags[2][world]      int64, written by rank q into slot [area][q]
-//   vals[2][world][2]    float64 partial sums, same indexing
+//   flags[3][world]      int64, written by rank q into slot [area][q]
+//   vals[3][world][2]    float64 partial sums, same indexing
 //   epoch                int64, bumped once per solve on every rank
 // trnsparse_peer_reduce_push replaces "all-reduce two doubles + halo
 // exchange" with one single-CTA kernel: push halo rows and the local partials
 // to every peer, fence, raise this rank's flag on every peer, wait (bounded)
 // for every peer's flag, then sum the partials in rank order, so every rank
 // gets bit-identical totals. Flags hold increasing sequence numbers
-// (epoch * stride + step + 1), so nothing is ever reset.
+// (epoch * stride + step + 1), so nothing is ever reset. Three areas: the
+// solve's setup exchange uses area 2 and iterations alternate 0 / 1, so two
+// consecutive exchanges never share an area (a rank may run one exchange
+// ahead of a peer, never two) — including across back-to-back solves.
 //
 // Plain stores and loads only: no TMA, no multicast.
 #include <string.h>
@@ -35,16 +38,16 @@ __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
 }
 
 struct CommArea {
-  long long* flags;  // [2][world]
-  double* vals;      // [2][world][2]
+  long long* flags;  // [3][world]
+  double* vals;      // [3][world][2]
   long long* epoch;
 };
 
 __device__ __forceinline__ CommArea area_of(char* base, size_t comm_off, int world) {
   CommArea a;
   a.flags = reinterpret_cast<long long*>(base + comm_off);
-  a.vals = reinterpret_cast<double*>(base + comm_off + 16 * world);
-  a.epoch = reinterpret_cast<long long*>(base + comm_off + 16 * world + 32 * world);
+  a.vals = reinterpret_cast<double*>(base + comm_off + 24 * world);
+  a.epoch = reinterpret_cast<long long*>(base + comm_off + 72 * world);
   return a;
 }
 
@@ -118,7 +121,7 @@ __global__ void bump_epoch_kernel(char* mine, size_t comm_off, int world) {
 
 using namespace tsb;
 
-extern "C" size_t trnsparse_peer_comm_bytes(int world) { return static_cast<size_t>(16 * world + 32 * world + 64); }
+extern "C" size_t trnsparse_peer_comm_bytes(int world) { return static_cast<size_t>(72 * world + 64); }
 
 extern "C" int trnsparse_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
   TSB_REQUIRE(bytes > 0 && ptr && ipc_handle, "peer_alloc: bad argument");
@@ -158,7 +161,7 @@ extern "C" int trnsparse_peer_reduce_push(void* const* peers, int world, int ran
                                           double* my_b, int area, long long stride, long long step,
                                           const float* src, const long long* sends, int n_sends, int chunk,
                                           void* stream) {
-  TSB_REQUIRE(peers && world > 0 && world <= kMaxWorld && rank >= 0 && rank < world && (area == 0 || area == 1),
+  TSB_REQUIRE(peers && world > 0 && world <= kMaxWorld && rank >= 0 && rank < world && area >= 0 && area <= 2,
               "peer_reduce_push: bad argument");
   TSB_REQUIRE(n_sends == 0 || (src && sends && chunk > 0 && chunk % 4 == 0), "peer_reduce_push: bad halo list");
   reduce_push_kernel<<<1, 256, 0, as_stream(stream)>>>(reinterpret_cast<char* const*>(peers), world, rank, comm_off,

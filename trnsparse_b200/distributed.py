@@ -155,7 +155,8 @@ class ShardedCG:
 
     transport="nccl": scalar all-reduces and halo exchanges are NCCL
     collectives / send-recv. transport="fused": the exchanges happen inside
-    the two solver kernels of an iteration (see trnsparse_bsr_cg_fused_*).
+    the two solver kernels of an iteration (see trnsparse_bsr_cg_fused_*);
+    transport="coop": the same in one cooperative kernel per iteration.
     transport="peer": the workspace lives in a CUDA
     IPC buffer every rank maps, and one single-CTA kernel per exchange pushes
     the halo rows and partial sums straight into the peers' memory over
@@ -196,17 +197,17 @@ class ShardedCG:
         self.ws_bytes = _lib.raw("trnsparse_bsr_cg_workspace_size")(n_ext, max_iter)
         self.transport = transport
         self._peer_ptrs: list[int] = []
-        if transport in ("peer", "fused"):
+        if transport in ("peer", "fused", "coop"):
             self._setup_peer(max_iter)
         elif transport == "nccl":
             self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
         else:
-            raise ValueError(f"transport must be 'nccl', 'peer' or 'fused', got {transport!r}")
+            raise ValueError(f"transport must be 'nccl', 'peer', 'fused' or 'coop', got {transport!r}")
         offs = (ctypes.c_size_t * 6)()
         _lib.call("trnsparse_bsr_cg_layout", n_ext, max_iter, offs)
         self.offs = list(offs)
         self.r_vec = self.ws[offs[2] : offs[2] + 4 * n_ext].view(torch.float32)
-        if transport in ("peer", "fused"):
+        if transport in ("peer", "fused", "coop"):
             self._build_sends()
         self.graph = None
         if graph:
@@ -281,7 +282,7 @@ class ShardedCG:
 
     def close(self) -> None:
         """Release the peer mappings and the shared buffer (peer transport)."""
-        if self.transport not in ("peer", "fused") or not hasattr(self, "_own_ptr"):
+        if self.transport not in ("peer", "fused", "coop") or not hasattr(self, "_own_ptr"):
             return
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
@@ -297,8 +298,8 @@ class ShardedCG:
     def _solve(self, check: bool) -> None:
         if self.transport == "peer":
             return self._solve_peer()
-        if self.transport == "fused":
-            return self._solve_fused()
+        if self.transport in ("fused", "coop"):
+            return self._solve_fused(coop=self.transport == "coop")
         lib, sh, ws, offs, g = self._lib, self.shard, self.ws, self.offs, self.group
         s = lib.stream_handle(self.dev)
         n_own, n_ext = sh.n_own, sh.n_ext
@@ -331,7 +332,7 @@ class ShardedCG:
         lib.call("trnsparse_bsr_cg_dist_start", sh.n_own, sh.n_ext, self.b.data_ptr(), inv, self.max_iter,
                  ws.data_ptr(), self.ws_bytes, s)
         slot = offs[1]
-        self._push(24, slot + 8, 1, 0, True)  # ||b||^2, r0.z0, halo of r0
+        self._push(24, slot + 8, 2, 0, True)  # ||b||^2, r0.z0, halo of r0 (area 2: setup only)
         for k in range(self.max_iter + 1):
             lib.call("trnsparse_bsr_cg_dist_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 0,
                      ws.data_ptr(), s)
@@ -342,7 +343,7 @@ class ShardedCG:
                      ws.data_ptr(), s)
             self._push(slot + 32 * k + 16, slot + 32 * k + 24, 1, 2 + 2 * k, True)  # r.r, r.z, halo of r
 
-    def _solve_fused(self) -> None:
+    def _solve_fused(self, coop: bool = False) -> None:
         lib, sh, ws = self._lib, self.shard, self.ws
         s = lib.stream_handle(self.dev)
         inv = lib.ptr(self.inv_d)
@@ -352,6 +353,10 @@ class ShardedCG:
         lib.call("trnsparse_bsr_cg_fused_start", sh.n_own, sh.n_ext, sh.block_size, self.b.data_ptr(), inv,
                  self.max_iter, ws.data_ptr(), self.ws_bytes, *peer, s)
         for k in range(self.max_iter + 1):
+            if coop:
+                lib.call("trnsparse_bsr_cg_coop_iter", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k,
+                         ws.data_ptr(), *peer, s)
+                continue
             lib.call("trnsparse_bsr_cg_fused_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 0,
                      ws.data_ptr(), *peer, s)
             if k == self.max_iter:
