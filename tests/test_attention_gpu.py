@@ -117,3 +117,23 @@ def test_attention_tensor_core_empty_block_row():
     for h in range(2):
         ref = oracle.block_sparse_attention(Q[0, h].float(), K[0, h].float(), V[0, h].float(), rp, ci, 128)
         assert rel_fro(got[0, h].float(), ref) <= 2e-2
+
+
+@pytest.mark.parametrize("scale", [0.9, -0.7])
+def test_attention_tensor_core_moving_max(scale):
+    """Key blocks of growing magnitude move the running row max on many steps,
+    so the in-TMEM rescale of the output runs; a negative scale flips the
+    max/min roles."""
+    from trnsparse_b200.ops import _attn_forward
+
+    seq, hd = 1024, 64
+    mask = w.sliding_window_mask(seq=seq, window=5, n_global=1)
+    Q, K, V = w.attention_inputs(heads=2, seq=seq, hd=hd, seed=21)
+    gain = torch.repeat_interleave(torch.linspace(0.1, 3.0, seq // 128), 128).view(1, 1, seq, 1)
+    K = (K.float() * gain).to(torch.bfloat16)
+    tc = _attn_forward(Q.cuda(), K.cuda(), V.cuda(), mask, scale)
+    assert ts._lib.device_error() == 0
+    for h in range(2):
+        ref = oracle.block_sparse_attention(Q[0, h].float(), K[0, h].float(), V[0, h].float(),
+                                            mask.block_row_ptrs, mask.block_col_indices, 128, scale=scale)
+        assert rel_fro(tc[0, h].float().cpu(), ref) <= 2e-2

@@ -1,9 +1,10 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers, bulk (TMA) copies, fences.
 //
-// Every wait is bounded: after kSpinLimit polls a wait gives up, records the
-// call site in the device error word (read by trnsparse_device_error) and
-// returns false, so a kernel can never hang the GPU on a barrier that is
-// never completed.
+// Every wait is bounded: an mbarrier wait gives up after kWaitNs of global
+// time (kSpinLimit polls for the flag spins of the multi-GPU solvers),
+// records the cause in the device error word (read by
+// trnsparse_device_error) and returns false, so a kernel can never hang the
+// GPU on a barrier that is never completed.
 #pragma once
 
 #include <stdint.h>
@@ -23,6 +24,13 @@ enum DeviceError : int {
 };
 
 constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s: pipeline stages complete in microseconds
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,10 +72,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitNs) break;
+  }
   record_device_error(DEVERR_MBAR_TIMEOUT);
   return false;
 }

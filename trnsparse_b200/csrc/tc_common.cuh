@@ -88,7 +88,8 @@ __global__ void transpose_b_kernel(int64_t n, int64_t k, const E* __restrict__ B
 inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
-                 uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows) {
+                 uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -104,8 +105,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uin
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TRNSPARSE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return TRNSPARSE_OK;
