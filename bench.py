@@ -370,7 +370,8 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
                                    "frac_of_peak": round(tfl / peak, 3),
                                    "peak": ("bf16 measured" if dt == torch.bfloat16 else "tf32 derived / 3 passes"),
                                    "l2": "flushed" if small else "inputs exceed L2",
-                                   "includes": "zeroing C, B transpose/split, tensor-core kernel"}
+                                   "includes": ("B split/transpose (fp32) or none (bf16), C clearing when a block-row is split, "
+                                                "tensor-core kernel")}
             del A, B, Bd
     # config 2b: CSR spmm, k = 32
     A = w.poisson2d_csr(2048)

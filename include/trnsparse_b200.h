@@ -164,17 +164,34 @@ TRNSPARSE_API int trnsparse_bsr_spmm_simt(int64_t m, int64_t n, int b, int64_t n
  * that nki_bsr_spmm replaces on Trainium (trnsparse/nki/dispatch.py:372-381).
  *   dtype F32: 3xTF32 (hi*hi + hi*lo + lo*hi); blocks_hi/blocks_lo are the
  *              tf32 split of the blocks (trnsparse_bsr_split_tf32); B, C fp32.
- *   dtype BF16: blocks_hi and B are bf16 (blocks_lo unused); C is fp32.
- * units: int32 triples (block_row, first_block, end_block) covering every
- * stored block exactly once, each within one block-row; n_units of them.
- * C (m x k, row stride ldc) is overwritten. bn: N tile (128 or 256; 0 =
- * choose). Workspace: trnsparse_bsr_spmm_tc_workspace_size(n, k, dtype)
- * bytes (B transposed to K-major, split for F32). */
+ *   dtype BF16: blocks_hi and B are bf16 (blocks_lo unused).
+ * c_dtype: F32, or BF16 (bf16 inputs and needs_zero == 0 only: the fp32
+ * accumulators are rounded once, in the epilogue).
+ * plan (device memory): the work schedule written on the host by
+ * trnsparse_bsr_spmm_tc_plan for this matrix's row pointers, k, bn and grid
+ * (CTA count; cache it per matrix). needs_zero: that call's flag (C is
+ * cleared first when a block-row is split across units).
+ * C (m x k, row stride ldc elements, rows 16-byte aligned) is overwritten. bn: N tile, 128 or 256 (the plan's). Workspace:
+ * trnsparse_bsr_spmm_tc_workspace_size(n, k, dtype) bytes (F32: B^T split;
+ * BF16: a padded copy of B, used only when B's rows are not 16-byte aligned
+ * or k < 64). */
 TRNSPARSE_API size_t trnsparse_bsr_spmm_tc_workspace_size(int64_t n, int64_t k, int dtype);
 TRNSPARSE_API int trnsparse_bsr_spmm_tc(int64_t m, int64_t n, int64_t n_blocks, const int* col_idx,
-                          const void* blocks_hi, const void* blocks_lo, int dtype, const int* units,
-                          int n_units, const void* B, int64_t k, int64_t ldb, float* C, int64_t ldc,
-                          int bn, void* ws, size_t ws_bytes, void* stream);
+                          const void* blocks_hi, const void* blocks_lo, int dtype, const int* plan,
+                          int grid, int needs_zero, const void* B, int64_t k, int64_t ldb, void* C,
+                          int64_t ldc, int c_dtype, int bn, void* ws, size_t ws_bytes, void* stream);
+
+/* Host-side work schedule for trnsparse_bsr_spmm_tc. row_ptr: the host copy
+ * of the n_block_rows + 1 block-row pointers. Units are (block-row, run of at
+ * most ~n_blocks * tiles / (3 n_ctas) of its blocks, N tile); they are
+ * assigned longest first to the least-loaded of min(n_ctas, units) CTAs.
+ * plan: host int32 buffer of `capacity` >= trnsparse_bsr_spmm_tc_plan_capacity
+ * entries; outputs the unit count, the grid and whether C needs clearing. */
+TRNSPARSE_API int64_t trnsparse_bsr_spmm_tc_plan_capacity(int64_t n_block_rows, int64_t n_blocks, int64_t k,
+                                                          int bn, int n_ctas);
+TRNSPARSE_API int trnsparse_bsr_spmm_tc_plan(int64_t n_block_rows, const int* row_ptr, int64_t k, int bn,
+                                             int n_ctas, int* plan, int64_t capacity, int* n_units,
+                                             int* grid, int* needs_zero);
 
 /* hi = tf32(src), lo = tf32(src - hi), elementwise over `count` floats
  * (round to nearest, ties away). Used once per BSR matrix for the F32

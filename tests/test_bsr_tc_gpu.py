@@ -90,3 +90,22 @@ def test_tc_bf16(k):
     assert got.dtype == torch.bfloat16
     assert rel_fro(got.float(), _ref(A, B)) <= 2e-2
     assert ts._lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype,k", [(torch.bfloat16, 40), (torch.bfloat16, 100), (torch.bfloat16, 600),
+                                     (torch.float32, 100), (torch.float32, 600)])
+def test_tc_whole_row_units(dtype, k):
+    """Enough busy block-rows that every unit is a whole block-row (plain TMA stores,
+    bf16 C written by the epilogue for bf16 inputs): ragged m, n and k, empty rows,
+    k below one 64-column box (padded B copy) and several N tiles."""
+    A = _random_bsr(200, 6, 0.3, seed=k, dtype=dtype, shape=(200 * 128 - 37, 6 * 128 - 5))
+    empty = (A.block_row_ptrs[1:] == A.block_row_ptrs[:-1]).nonzero().flatten().tolist()
+    assert len(empty) > 0 and 200 - len(empty) >= 148
+    B = torch.randn(A.shape[1], k, generator=torch.Generator().manual_seed(k)).to(dtype)
+    got = ts.bsr_spmm(A, B.cuda())
+    assert got.dtype == dtype and got.shape == (A.shape[0], k)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    assert rel_fro(got.float(), _ref(A, B)) <= tol
+    for r in empty[:5]:
+        assert torch.count_nonzero(got[r * 128:(r + 1) * 128]) == 0
+    assert ts._lib.device_error() == 0

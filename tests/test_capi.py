@@ -41,3 +41,69 @@ def test_error_reporting_without_gpu():
     assert b"negative" in lib.trnsparse_last_error()
     assert lib.trnsparse_version() >= 100
     assert isinstance(lib, ctypes.CDLL)
+
+
+def _plan(row_ptr, k, bn, ctas):
+    import torch
+
+    rp = torch.tensor(row_ptr, dtype=torch.int32)
+    R = len(row_ptr) - 1
+    cap = _lib.raw("trnsparse_bsr_spmm_tc_plan_capacity")(R, row_ptr[-1], k, bn, ctas)
+    plan = torch.zeros(cap, dtype=torch.int32)
+    nu, grid, zero = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _lib.call("trnsparse_bsr_spmm_tc_plan", R, rp.data_ptr(), k, bn, ctas, plan.data_ptr(), cap,
+              ctypes.byref(nu), ctypes.byref(grid), ctypes.byref(zero))
+    g = grid.value
+    head = (g + 4) & ~3
+    offs = plan[: g + 1].tolist()
+    units = plan[head: head + 4 * nu.value].view(-1, 4).tolist()
+    return offs, units, g, zero.value
+
+
+def test_spmm_tc_plan_covers_every_block_once_per_tile():
+    """Host scheduler of the tensor-core bsr_spmm (no GPU): every stored block is in
+    exactly one unit per N tile, units stay inside their block-row, empty block-rows
+    get a zero-storing unit, reduce-add only where a block-row is split, and the CTA
+    offsets partition the unit list."""
+    import random
+
+    rng = random.Random(5)
+    for R, ctas, k, bn in [(16, 148, 256, 256), (128, 148, 512, 256), (7, 4, 100, 128), (300, 148, 64, 128),
+                           (3, 148, 1000, 256)]:
+        lens = [0 if rng.random() < 0.15 else rng.randint(1, 40) for _ in range(R)]
+        rp = [0]
+        for L in lens:
+            rp.append(rp[-1] + L)
+        offs, units, g, zero = _plan(rp, k, bn, ctas)
+        tiles = -(-k // bn)
+        assert 1 <= g <= ctas and offs[0] == 0 and offs[-1] == len(units)
+        assert all(a <= b for a, b in zip(offs, offs[1:]))
+        seen = {}
+        split_rows = set()
+        for row, b0, b1, w in units:
+            tile, reduce = w & ~(1 << 30), bool(w & (1 << 30))
+            assert 0 <= tile < tiles and rp[row] <= b0 <= b1 <= rp[row + 1]
+            if reduce:
+                split_rows.add(row)
+            if lens[row] == 0:
+                assert b0 == b1 and not reduce
+            for b in range(b0, b1):
+                seen[(b, tile)] = seen.get((b, tile), 0) + 1
+        assert seen == {(b, t): 1 for b in range(rp[-1]) for t in range(tiles)}
+        for row in range(R):
+            n_units = sum(1 for u in units if u[0] == row)
+            assert n_units >= tiles
+            assert (row in split_rows) == (n_units > tiles)
+        assert zero == (1 if split_rows else 0)
+
+
+def test_spmm_tc_plan_rejects_small_buffer():
+    import torch
+
+    rp = torch.tensor([0, 3, 5], dtype=torch.int32)
+    plan = torch.zeros(4, dtype=torch.int32)
+    nu, grid, zero = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    rc = _lib.load().trnsparse_bsr_spmm_tc_plan(2, ctypes.c_void_p(rp.data_ptr()), 256, 256, 148,
+                                               ctypes.c_void_p(plan.data_ptr()), 4, ctypes.byref(nu),
+                                               ctypes.byref(grid), ctypes.byref(zero))
+    assert rc == _lib.ERR_ARG

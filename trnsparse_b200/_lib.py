@@ -48,7 +48,10 @@ SIGNATURES.update({
     "trnsparse_bsr_power_finish": [_i64, _p, _i32, _p, _p],
     "trnsparse_bsr_spmm_simt": _BSR + [_p, _i64, _i64, _p, _i64, _p],
     "trnsparse_bsr_spmm_tc_workspace_size": [_i64, _i64, _i32],
-    "trnsparse_bsr_spmm_tc": [_i64, _i64, _i64, _p, _p, _p, _i32, _p, _i32, _p, _i64, _i64, _p, _i64, _i32, _p, _sz, _p],
+    "trnsparse_bsr_spmm_tc_plan_capacity": [_i64, _i64, _i64, _i32, _i32],
+    "trnsparse_bsr_spmm_tc_plan": [_i64, _p, _i64, _i32, _i32, _p, _i64, _p, _p, _p],
+    "trnsparse_bsr_spmm_tc": [_i64, _i64, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _p, _i64, _i64, _p, _i64, _i32,
+                              _i32, _p, _sz, _p],
     "trnsparse_bsr_split_tf32": [_i64, _p, _p, _p, _p],
     "trnsparse_screened_spmm_workspace_size": [_i64, _i64],
     "trnsparse_screened_spmm": [_i64, _i64, _i64, _p, _i64, _p, _i32, _i64, _f64, _p, _i64, _p, _i64, _p, _sz, _p],
@@ -75,6 +78,7 @@ _RESTYPE = {
     "trnsparse_bsr_cg_workspace_size": C.c_size_t,
     "trnsparse_bsr_power_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_workspace_size": C.c_size_t,
+    "trnsparse_bsr_spmm_tc_plan_capacity": C.c_int64,
     "trnsparse_screened_spmm_workspace_size": C.c_size_t,
     "trnsparse_peer_comm_bytes": C.c_size_t,
 }

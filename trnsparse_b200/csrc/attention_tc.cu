@@ -82,23 +82,6 @@ struct AtBars {
   int abort_flag;
 };
 
-// MN-major, 128-byte-swizzled operand (V as B of O += P V): 8-row atoms along
-// K at 1024 bytes (SBO), 64-wide N chunks at `lbo` bytes (LBO).
-__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t saddr, uint32_t lbo) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>(1024u >> 4) << 32;
-  d |= static_cast<uint64_t>(1u) << 46;
-  d |= static_cast<uint64_t>(2u) << 61;
-  return d;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
 // 2^x on the special-function unit (PTX ex2.approx.ftz.f32).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

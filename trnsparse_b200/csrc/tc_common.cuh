@@ -5,6 +5,7 @@
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 #include <stdlib.h>
 
 #include "common.cuh"
@@ -33,6 +34,12 @@ __device__ __forceinline__ void red_add_v4(float* p, uint32_t a, uint32_t b, uin
 }
 __device__ __forceinline__ void red_add(float* p, uint32_t a) {
   asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(p), "f"(__uint_as_float(a)) : "memory");
+}
+
+// Two floats -> one 32-bit word of bf16 (round to nearest even), a in the low half.
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 // ---------------------------------------------------------------- prep kernels

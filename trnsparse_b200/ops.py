@@ -10,6 +10,8 @@ compute path and no backend switch.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -195,25 +197,31 @@ def _sm_count(dev: torch.device) -> int:
     return torch.cuda.get_device_properties(dev).multi_processor_count
 
 
-def _tc_plan(A: BSRMatrix, lay: dict, dev: torch.device, k: int) -> tuple[torch.Tensor, int, int]:
-    """Work units (block_row, first, end) for the tensor-core kernel, cached per N tiling.
+def _tc_plan(A: BSRMatrix, lay: dict, dev: torch.device, k: int) -> tuple[torch.Tensor, int, int, int]:
+    """Work schedule for the tensor-core kernel, cached per (matrix, N tiling, k tiles).
 
-    The N tile is 128 or 256 columns; the stored blocks of a block-row are
-    split into runs of G blocks, with G chosen so the grid covers the SMs
-    about once (each CTA holds one SM: ~193 KB of shared memory).
+    Built on the host by the library (trnsparse_bsr_spmm_tc_plan): units of
+    (block-row, run of its blocks, N tile), longest first onto the
+    least-loaded of one persistent CTA per SM. Returns (plan on the device,
+    grid, needs_zero, bn).
     """
     sms = _sm_count(dev)
     bn = 128 if k <= 128 else 256  # wide tiles read each A block once per 256 columns
-    n_tiles = -(-k // bn)
-    key = ("tc_units", bn)
+    key = ("tc_plan", bn, -(-k // bn))
     hit = lay.get(key)
     if hit is not None:
         return hit
-    G = max(1, round(A.n_blocks * n_tiles / sms))
-    rp = lay["host_row_ptr"].tolist()
-    units = [(i, s, min(s + G, rp[i + 1])) for i in range(len(rp) - 1) for s in range(rp[i], rp[i + 1], G)]
-    t = torch.tensor(units, dtype=torch.int32).reshape(-1, 3).to(dev)
-    lay[key] = (t, len(units), bn)
+    rp = lay["host_row_ptr"].to(torch.int32).contiguous()
+    R = rp.numel() - 1
+    cap = _lib.raw("trnsparse_bsr_spmm_tc_plan_capacity")(R, A.n_blocks, k, bn, sms)
+    if cap < 0:
+        raise ValueError("bsr_spmm: cannot plan this shape")
+    plan = torch.empty(cap, dtype=torch.int32)
+    n_units, grid, zero = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _lib.call("trnsparse_bsr_spmm_tc_plan", R, rp.data_ptr(), k, bn, sms, plan.data_ptr(), cap,
+              ctypes.byref(n_units), ctypes.byref(grid), ctypes.byref(zero))
+    used = ((grid.value + 4) & ~3) + 4 * n_units.value
+    lay[key] = (plan[:used].to(dev), grid.value, zero.value, bn)
     return lay[key]
 
 
@@ -254,8 +262,10 @@ def bsr_spmm(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
         if A.block_size == 128 and k > 1 and A.n_blocks > 0:
             bf16 = A.dtype == torch.bfloat16
             Bd = _on(B, dev, torch.bfloat16 if bf16 else torch.float32)
-            out = torch.empty(m, k, dtype=torch.float32, device=dev)
-            units, n_units, bn = _tc_plan(A, lay, dev, k)
+            plan, grid, zero, bn = _tc_plan(A, lay, dev, k)
+            direct = bf16 and not zero  # bf16 C straight from the epilogue
+            kp = -(-k // 8) * 8 if direct else -(-k // 4) * 4  # 16-byte C rows for the TMA stores
+            out = torch.empty(m, kp, dtype=torch.bfloat16 if direct else torch.float32, device=dev)
             if bf16:
                 (hi, lo), code = (lay["blocks"], None), _lib.BF16
             else:
@@ -263,9 +273,11 @@ def bsr_spmm(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
             ws_bytes = _lib.raw("trnsparse_bsr_spmm_tc_workspace_size")(n, k, code)
             ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
             _lib.call("trnsparse_bsr_spmm_tc", m, n, A.n_blocks, lay["col_idx"].data_ptr(), hi.data_ptr(),
-                      _lib.ptr(lo), code, units.data_ptr(), n_units, Bd.data_ptr(), k, k, out.data_ptr(), k, bn,
-                      ws.data_ptr(), ws_bytes, s)
-            return _back(out.to(A.dtype) if bf16 else out, B)
+                      _lib.ptr(lo), code, plan.data_ptr(), grid, zero, Bd.data_ptr(), k, k, out.data_ptr(), kp,
+                      _lib.BF16 if direct else _lib.F32, bn, ws.data_ptr(), ws_bytes, s)
+            if kp != k:
+                out = out[:, :k].contiguous()
+            return _back(out.to(A.dtype), B)
         Bd = _on(B, dev, torch.float32)
         out = torch.empty(m, k, dtype=torch.float32, device=dev)
         geo = _bsr_geometry(A, dev)
