@@ -275,13 +275,32 @@ def run_ours(args, ws, rank, local):
         sharded = run_sharded_cg(ws, rank, local, pk)
         if rank == 0:
             line["extra_sharded"] = sharded
+    elif not args.no_extra:
+        # the same sharded solvers on one rank: the N = 1 point of their scaling curve
+        import socket
+
+        import torch.distributed as dist
+
+        sock = socket.socket()
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+        sock.close()
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                device_id=torch.device("cuda", local))
+        try:
+            line["extra_sharded"] = run_sharded_cg(1, 0, local, pk, transports=("cgcg", "coop"))
+        finally:
+            dist.destroy_process_group()
     return line
 
 
-def run_sharded_cg(ws: int, rank: int, local: int, pk: dict) -> dict:
+def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
+                   transports: tuple = ("cgcg", "coop", "fused", "peer", "nccl")) -> dict:
     """Config 5 on ws GPUs: block-row-sharded Jacobi-PCG (strong scaling: the
-    2048-block-row matrix is split across the ranks), peer-memory transport,
-    whole solve captured in one CUDA graph. 30 iterations, all of which do
+    2048-block-row matrix is split across the ranks), each transport (cgcg:
+    one reduction per iteration in one cooperative launch; coop / fused /
+    peer / nccl: the reference's two reductions), whole solve captured in one
+    CUDA graph. 30 iterations, all of which do
     work (the reference's loop breaks on |p.Ap| < 1e-30 near iteration 31
     for this matrix); time = max over ranks."""
     import torch.distributed as dist
@@ -294,19 +313,23 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict) -> dict:
     bl = b[sh.r0 * 128 : sh.r1 * 128].cuda()
     iters = 30
     out = {}
-    for transport in ("coop", "fused", "peer", "nccl"):
-        cg = D.ShardedCG(sh, bl, tol=0.0, max_iter=iters, graph=True, transport=transport)
-        cg.run()
-        torch.cuda.synchronize()
-        dist.barrier()
-        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        x, it, rel = cg.run()
-        e.record()
-        torch.cuda.synchronize()
-        ms = max_over_ranks(a.elapsed_time(e), ws)
-        executed = cg.executed_iterations()
-        cg.close()
+    for transport in transports:
+        try:
+            cg = D.ShardedCG(sh, bl, tol=0.0, max_iter=iters, graph=True, transport=transport)
+            cg.run()
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            x, it, rel = cg.run()
+            e.record()
+            torch.cuda.synchronize()
+            ms = max_over_ranks(a.elapsed_time(e), ws)
+            executed = cg.executed_iterations()
+            cg.close()
+        except Exception as exc:  # one transport failing must not lose the others' numbers
+            out[f"config5_cg_sharded_{transport}"] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
+            continue
         nb = A.n_blocks * 128 * 128 * 4
         out[f"config5_cg_sharded_{transport}"] = {
             "us_per_iteration": round(ms / max(executed, 1) * 1e3, 2), "iterations": executed,

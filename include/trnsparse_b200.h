@@ -304,14 +304,35 @@ TRNSPARSE_API int trnsparse_bsr_cg_fused_phase(int64_t m, int64_t n, int b, int6
                                  int world, int rank, size_t comm_off, const long long* sends, int n_sends,
                                  void* stream);
 
-/* One cooperative launch per iteration of the fused sharded CG: the two
- * phases of trnsparse_bsr_cg_fused_phase merged (iteration k; k == max_iter
- * only records the final status). Same buffers, protocol and requirements as
+/* The fused sharded CG in one cooperative launch for iterations k_begin ..
+ * k_end (k == max_iter only records the final status): every iteration's
+ * two phases run back to back inside the kernel, the peer flags serving as
+ * the grid-wide barrier. Same buffers, protocol and requirements as
  * trnsparse_bsr_cg_fused_*; start with trnsparse_bsr_cg_fused_start. */
-TRNSPARSE_API int trnsparse_bsr_cg_coop_iter(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+TRNSPARSE_API int trnsparse_bsr_cg_coop_run(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
                                const int* col_idx, const float* blocks, float* x, const float* inv_d,
-                               double tol, int max_iter, int k, void* ws, void* const* peers, int world,
-                               int rank, size_t comm_off, const long long* sends, int n_sends, void* stream);
+                               double tol, int max_iter, int k_begin, int k_end, void* ws, void* const* peers,
+                               int world, int rank, size_t comm_off, const long long* sends, int n_sends,
+                               void* stream);
+
+/* Sharded Jacobi-PCG with one reduction per iteration (Chronopoulos-Gear
+ * recurrences; the same iterates as the reference's cg_bsr in exact
+ * arithmetic, trnsparse/iterative.py:53-126), whole solve in one
+ * cooperative launch after a small start kernel, exchanges over the peer
+ * buffers of trnsparse_peer_* (CUDA IPC, one NVLink box). Every rank's
+ * workspace holds n_alloc entries per vector (the largest n_ext of all
+ * ranks), laid out per trnsparse_bsr_cgcg_layout, at byte offset ws_off of its
+ * peer buffer; sends: n_sends triples (source element, destination rank,
+ * destination element) of the b-row halo chunks this rank owes. x0 = 0;
+ * inv_d (n_ext, halo filled) or null. Status record and slots as for the
+ * other CG entry points (slot k: p.Ap, gamma, delta, r.r). */
+TRNSPARSE_API size_t trnsparse_bsr_cgcg_workspace_size(int64_t n_alloc, int max_iter);
+TRNSPARSE_API int trnsparse_bsr_cgcg_layout(int64_t n_alloc, int max_iter, size_t* offsets /* 9 */);
+TRNSPARSE_API int trnsparse_bsr_cgcg_solve(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                               const int* col_idx, const float* blocks, const float* b_vec, float* x,
+                               const float* inv_d, double tol, int max_iter, int64_t n_alloc, void* ws,
+                               size_t ws_off, size_t ws_bytes, void* const* peers, int world, int rank,
+                               size_t comm_off, const long long* sends, int n_sends, void* stream);
 
 /* Allocation-free PCG. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (code running inside an

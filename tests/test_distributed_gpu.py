@@ -1,6 +1,7 @@
-"""Block-row-sharded Jacobi-PCG on 2 GPUs (NCCL) against the single-GPU solve.
+"""Block-row-sharded Jacobi-PCG on 1 and 2 GPUs against the single-GPU solve.
 
-Runs as two spawned processes, one per GPU; skipped with fewer than 2 GPUs.
+Runs as spawned processes, one per GPU; the 2-GPU cases are skipped with
+fewer than 2 GPUs.
 Tolerance: 1e-5 relative Frobenius error on the assembled solution.
 """
 
@@ -37,7 +38,8 @@ def _worker(rank, world, port, cases, out, transport="nccl"):
             A, b = w.block_pentadiagonal_spd(nbr)
             sh = D.shard_bsr(A, rank, world)
             bl = b[sh.r0 * 128 : sh.r1 * 128].cuda()
-            cg = D.ShardedCG(sh, bl, tol=tol, max_iter=max_iter, transport=transport, graph=(transport != "nccl"))
+            cg = D.ShardedCG(sh, bl, tol=tol, max_iter=max_iter, transport=transport,
+                             graph=(transport != "nccl" and tol <= 0))
             x, it, rel = cg.run()
             x2, it2, rel2 = cg.run()  # a second solve on the same buffers gives the same answer
             assert (torch.linalg.norm(x - x2) / torch.linalg.norm(x)).item() <= 1e-6 and it == it2
@@ -53,14 +55,19 @@ def _worker(rank, world, port, cases, out, transport="nccl"):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["nccl", "peer", "fused", "coop"])
-def test_sharded_cg_two_gpus(transport):
+@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "fused", "coop", "cgcg"])
+def test_sharded_cg(transport, world):
+    """world 1 runs the same sharded machinery (own flags, no halo) on one GPU."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     cases = [(64, 0.0, 30), (96, 1e-6, 100)] if transport == "nccl" else [(64, 0.0, 30), (96, 0.0, 40)]
+    if transport == "cgcg":
+        cases.append((80, 1e-6, 100))  # converges before max_iter: the tolerance exit
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    mp.start_processes(_worker, args=(2, _free_port(), cases, out, transport), nprocs=2, start_method="spawn",
-                       join=True)
+    mp.start_processes(_worker, args=(world, _free_port(), cases, out, transport), nprocs=world,
+                       start_method="spawn", join=True)
     for ci in range(len(cases)):
         err, it, itr, rel, relr = out[ci]
         assert err <= 1e-5, out[ci]

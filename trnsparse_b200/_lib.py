@@ -70,7 +70,11 @@ SIGNATURES.update({
                                    _i32, _p],
     "trnsparse_bsr_cg_fused_start": [_i64, _i64, _i32, _p, _p, _i32, _p, _sz, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_fused_phase": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
-    "trnsparse_bsr_cg_coop_iter": _BSR + [_p, _p, _f64, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
+    "trnsparse_bsr_cgcg_workspace_size": [_i64, _i32],
+    "trnsparse_bsr_cgcg_layout": [_i64, _i32, _p],
+    "trnsparse_bsr_cgcg_solve": _BSR + [_p, _p, _p, _f64, _i32, _i64, _p, _sz, _sz, _p, _i32, _i32, _sz, _p, _i32,
+                                        _p],
+    "trnsparse_bsr_cg_coop_run": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_noalloc": _BSR + [_p, _p, _i32, _p, _f64, _i32, _p, _p],
 })
 _RESTYPE = {
@@ -78,6 +82,7 @@ _RESTYPE = {
     "trnsparse_bsr_cg_workspace_size": C.c_size_t,
     "trnsparse_bsr_power_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_workspace_size": C.c_size_t,
+    "trnsparse_bsr_cgcg_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_plan_capacity": C.c_int64,
     "trnsparse_screened_spmm_workspace_size": C.c_size_t,
     "trnsparse_peer_comm_bytes": C.c_size_t,

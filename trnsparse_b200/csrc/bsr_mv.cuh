@@ -56,13 +56,41 @@ __device__ __forceinline__ void run_tail(const Op& op) {
   if constexpr (HasTail<Op>::value) op.tail();
 }
 
-template <class Op>
+#ifdef TSB_CG_TRACE
+// Timing probe (compile-time only): CTA 0 of each launch takes a slot and
+// stamps entry, after begin(), before finish() and after the tail.
+extern __device__ unsigned long long g_cg_trace[512][8];
+extern __device__ unsigned g_cg_trace_n;
+__device__ __forceinline__ unsigned long long cgt_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define CGT_ENTER                                                              \
+  __shared__ unsigned cgt_slot;                                                \
+  if (blockIdx.x == 0 && threadIdx.x == 0) {                                   \
+    cgt_slot = atomicAdd(&g_cg_trace_n, 1u) & 511u;                            \
+    g_cg_trace[cgt_slot][0] = cgt_now();                                       \
+  }
+#define CGT(i) \
+  if (blockIdx.x == 0 && threadIdx.x == 0) g_cg_trace[cgt_slot][i] = cgt_now()
+#else
+#define CGT_ENTER
+#define CGT(i)
+#endif
+
+// KEEP: load the blocks with the default L2 policy (a matrix that fits in L2
+// stays there across the iterations of a solver); otherwise stream them
+// (evict-first), so a larger-than-L2 matrix does not flush the vectors.
+template <class Op, bool KEEP = false>
 __global__ void __launch_bounds__(256)
 bsr128_mv_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_idx,
                  const float4* __restrict__ blocks, int n_block_rows, Op op) {
   __shared__ float ys[128];
   __shared__ double red[8];
+  CGT_ENTER
   if (!op.begin(blockIdx.x)) return;
+  CGT(1);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   double d0 = 0.0, d1 = 0.0;
   // one block-row per iteration; the grid may be smaller than the number of
@@ -78,7 +106,7 @@ bsr128_mv_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_id
       const float4* bp = blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
       float4 a[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) a[r] = __ldcs(bp + r * 32);
+      for (int r = 0; r < 16; ++r) a[r] = KEEP ? __ldg(bp + r * 32) : __ldcs(bp + r * 32);
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
         acc[r] = fmaf(a[r].x, xv.x, acc[r]);
@@ -102,7 +130,9 @@ bsr128_mv_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_id
     if (Op::kDots > 1) t1 = block_sum256(d1, red);
     if (threadIdx.x == 0) op.finish(t0, t1);
   }
+  CGT(2);
   run_tail(op);
+  CGT(3);
 }
 
 template <class Op>
@@ -151,17 +181,32 @@ struct BsrDesc {
   int64_t block_rows() const { return (m + b - 1) / b; }
 };
 
+// Whether `bytes` of matrix blocks can stay resident in this device's L2
+// across solver iterations (three quarters of it, leaving room for vectors).
+inline bool fits_l2(size_t bytes) {
+  static int l2 = -1;
+  if (l2 < 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrL2CacheSize, dev) != cudaSuccess)
+      v = 0;
+    l2 = v;
+  }
+  return bytes * 4 <= static_cast<size_t>(l2) * 3;
+}
+
 // Launches the right kernel for `d`; `vec_ok` says the Op's x4 may be used.
 // max_ctas > 0 caps the fast kernel's grid (persistent CTAs looping over block-rows).
 template <class Op>
-int launch_bsr_mv(const BsrDesc& d, const Op& op, bool vec_ok, cudaStream_t st, const char* what, int64_t max_ctas = 0) {
+int launch_bsr_mv(const BsrDesc& d, const Op& op, bool vec_ok, cudaStream_t st, const char* what, int64_t max_ctas = 0,
+                  bool keep_l2 = false) {
   if (d.fast() && vec_ok) {
     const int64_t nbr = d.block_rows();
     int64_t g = nbr;
     if (max_ctas > 0 && g > max_ctas) g = max_ctas;
-    if (g > 0)
-      bsr128_mv_kernel<Op><<<(unsigned)g, 256, 0, st>>>(d.row_ptr, d.col_idx,
-                                                       reinterpret_cast<const float4*>(d.blocks), (int)nbr, op);
+    if (g > 0) {
+      auto kern = keep_l2 ? bsr128_mv_kernel<Op, true> : bsr128_mv_kernel<Op, false>;
+      kern<<<(unsigned)g, 256, 0, st>>>(d.row_ptr, d.col_idx, reinterpret_cast<const float4*>(d.blocks), (int)nbr, op);
+    }
   } else {
     const int64_t g = (d.m + 255) / 256;
     if (g > 0) bsr_generic_mv_kernel<Op><<<(unsigned)g, 256, 0, st>>>(d.m, d.n, d.b, d.row_ptr, d.col_idx, d.blocks, op);

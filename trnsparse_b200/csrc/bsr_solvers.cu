@@ -96,14 +96,18 @@ struct PlainOp {
 template <class Op>
 __global__ void __launch_bounds__(256) vec_kernel(int64_t n, Op op) {
   __shared__ double red[8];
+  CGT_ENTER
   if (!op.begin(blockIdx.x)) return;
+  CGT(1);
   double d0 = 0.0, d1 = 0.0;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < n; i += static_cast<int64_t>(gridDim.x) * 256)
     op.elem(i, &d0, &d1);
   const double t0 = block_sum256(d0, red);
   const double t1 = block_sum256(d1, red);
   if (threadIdx.x == 0) op.finish(t0, t1);
+  CGT(2);
   run_tail(op);
+  CGT(3);
 }
 
 inline unsigned vec_grid(int64_t n) {
@@ -682,6 +686,7 @@ struct PeerCtx {
   long long stride;
   const long long* sends;  // halo r rows: (src elem offset, dst rank, dst byte offset)
   int n_sends, chunk;
+  long long seq0;  // epoch * stride once known (a one-launch solve reads the epoch once), else -1
 };
 
 __device__ __forceinline__ long long* pc_flags(const PeerCtx& p, char* base) {
@@ -691,13 +696,16 @@ __device__ __forceinline__ double* pc_vals(const PeerCtx& p, char* base) {
   return reinterpret_cast<double*>(base + p.comm_off + 24 * p.world);
 }
 __device__ __forceinline__ long long* pc_epoch(const PeerCtx& p, char* base) {
-  return reinterpret_cast<long long*>(base + p.comm_off + 72 * p.world);
+  return reinterpret_cast<long long*>(base + p.comm_off + 120 * p.world);
 }
 __device__ __forceinline__ unsigned int* pc_ticket(const PeerCtx& p, int which) {
-  return reinterpret_cast<unsigned int*>(p.peers[p.rank] + p.comm_off + 72 * p.world + 8) + which;
+  return reinterpret_cast<unsigned int*>(p.peers[p.rank] + p.comm_off + 120 * p.world + 8) + which;
+}
+__device__ __forceinline__ long long pc_seq_base(const PeerCtx& p) {
+  return (*reinterpret_cast<volatile long long*>(pc_epoch(p, p.peers[p.rank]))) * p.stride;
 }
 __device__ __forceinline__ long long pc_seq(const PeerCtx& p, long long step) {
-  return (*reinterpret_cast<volatile long long*>(pc_epoch(p, p.peers[p.rank]))) * p.stride + step + 1;
+  return (p.seq0 >= 0 ? p.seq0 : pc_seq_base(p)) + step + 1;
 }
 
 __device__ __forceinline__ long long ld_acq_sys(const long long* q) {
@@ -728,11 +736,11 @@ __device__ double2 pc_wait_sum(const PeerCtx& p, int area, long long step) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const volatile double* v = pc_vals(p, mine) + area * p.world * 2;
+    const volatile double* v = pc_vals(p, mine) + area * p.world * 4;
     double a = 0.0, b = 0.0;
     for (int q = 0; q < p.world; ++q) {
-      a += v[2 * q];
-      b += v[2 * q + 1];
+      a += v[4 * q];
+      b += v[4 * q + 1];
     }
     tot = make_double2(a, b);
   }
@@ -748,16 +756,18 @@ __device__ void pc_publish(const PeerCtx& p, int which, int area, long long step
   __shared__ double2 part;
   __syncthreads();  // every thread's stores of this CTA precede the ticket
   if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned t = atomicAdd(pc_ticket(p, which), 1u);
+    // acq_rel: releases this CTA's stores (ordered before by the barrier); the last CTA
+    // acquires every other CTA's
+    unsigned t;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;\n" : "=r"(t) : "l"(pc_ticket(p, which)) : "memory");
     last = ((t + 1) % gridDim.x) == 0;
-    if (last) {
-      __threadfence();
-      part = make_double2(a ? *(volatile const double*)a : 0.0, b ? *(volatile const double*)b : 0.0);
-    }
+    if (last) part = make_double2(a ? *(volatile const double*)a : 0.0, b ? *(volatile const double*)b : 0.0);
   }
   __syncthreads();
   if (!last) return;
+#ifdef TSB_CG_TRACE
+  if (threadIdx.x == 0) g_cg_trace[(g_cg_trace_n - 1) & 511u][4] = cgt_now();
+#endif
   const long long seq = pc_seq(p, step);
   if (halo) {
     for (int s = 0; s < p.n_sends; ++s) {
@@ -771,13 +781,16 @@ __device__ void pc_publish(const PeerCtx& p, int which, int area, long long step
     }
   }
   if (threadIdx.x < p.world) {
-    double* v = pc_vals(p, p.peers[threadIdx.x]) + (area * p.world + p.rank) * 2;
+    double* v = pc_vals(p, p.peers[threadIdx.x]) + (area * p.world + p.rank) * 4;
     v[0] = part.x;
     v[1] = part.y;
   }
-  __threadfence_system();
+  // the halo and partial stores above happen-before (barrier) the flag's release at system scope
   __syncthreads();
   if (threadIdx.x < p.world) st_rel_sys(pc_flags(p, p.peers[threadIdx.x]) + area * p.world + p.rank, seq);
+#ifdef TSB_CG_TRACE
+  if (threadIdx.x == 0) g_cg_trace[(g_cg_trace_n - 1) & 511u][5] = cgt_now();
+#endif
 }
 
 // step numbering: 0 = setup, 1 + 2k = p.Ap of iteration k, 2 + 2k = r.r / r.z of iteration k
@@ -915,14 +928,14 @@ struct CgUpdateFused {
 };
 
 __global__ void fused_bump_epoch(char* const* peers, int rank, size_t comm_off, int world) {
-  *reinterpret_cast<long long*>(peers[rank] + comm_off + 72 * world) += 1;
+  *reinterpret_cast<long long*>(peers[rank] + comm_off + 120 * world) += 1;
 }
 
 }  // namespace
 }  // namespace tsb
 
 #define PEER_ARGS void* const* peers, int world, int rank, size_t comm_off, const long long* sends, int n_sends
-#define PEER_CTX PeerCtx{reinterpret_cast<char* const*>(peers), world, rank, comm_off, 2ll * max_iter + 4, sends, n_sends, b}
+#define PEER_CTX PeerCtx{reinterpret_cast<char* const*>(peers), world, rank, comm_off, 2ll * max_iter + 4, sends, n_sends, b, -1}
 
 extern "C" int trnsparse_bsr_cg_fused_start(int64_t n_own, int64_t n_ext, int b, const float* b_vec,
                                             const float* inv_d, int max_iter, void* ws, size_t ws_bytes, PEER_ARGS,
@@ -957,104 +970,579 @@ extern "C" int trnsparse_bsr_cg_fused_phase(int64_t m, int64_t n, int b, int64_t
   if (phase == 0) {
     CgMvFused mv{inv_d, w, pprev, pcur, k, max_iter, tol, m, PEER_CTX, 0.f};
     // persistent CTAs: every CTA pays the peer-flag wait of its prologue once
-    return launch_bsr_mv(d, mv, all_aligned({inv_d, w.r, w.p0, w.p1}), st, "bsr_cg_fused mv", 3 * sm_count());
+    return launch_bsr_mv(d, mv, all_aligned({inv_d, w.r, w.p0, w.p1}), st, "bsr_cg_fused mv", 3 * sm_count(),
+                         fits_l2(static_cast<size_t>(n_blocks) * 128 * 128 * 4));
   }
   if (k >= max_iter) return TRNSPARSE_OK;
   return launch_vec(m, CgUpdateFused{inv_d, x, w, pcur, k, max_iter, PEER_CTX, 0.f}, st, "bsr_cg_fused update",
                     sm_count());
 }
 
-// ---------------------------------------------------------------- sharded CG, one kernel per iteration
-// The two fused kernels of an iteration merged into one cooperative launch
-// (all CTAs co-resident): prologue waits for the previous iteration's
-// r.r / r.z and halo, SpMV with p on the fly, last CTA publishes p.Ap, every
-// CTA waits for the global p.Ap, updates x and r on the rows it computed and
-// the last CTA publishes r.r / r.z and the halo rows of r.
+// ---------------------------------------------------------------- sharded CG, one kernel per solve
+// The two fused kernels of every iteration merged into one cooperative
+// launch (all CTAs co-resident) that loops over the iterations: each
+// iteration's prologue waits for the previous r.r / r.z and halo, the SpMV
+// computes p on the fly, the last CTA publishes p.Ap, every CTA waits for the
+// global p.Ap, updates x and r on its block-rows, and the last CTA publishes
+// r.r / r.z and the halo rows of r. The peer flags double as the grid-wide
+// barrier between the phases (each rank's own flag is raised by its last CTA
+// only after every CTA has taken its ticket), so no launch boundary remains.
 namespace tsb {
 namespace {
 
-__global__ void __launch_bounds__(256)
-cg_iter_coop_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_idx,
-                    const float4* __restrict__ blocks, int n_block_rows, CgMvFused mv, CgUpdateFused up) {
+template <bool KEEP>
+__global__ void __launch_bounds__(256, 2)  // two CTAs per SM: every block-row in flight at once
+cg_solve_coop_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_idx,
+                     const float4* __restrict__ blocks, int n_block_rows, CgMvFused mv, CgUpdateFused up,
+                     float* p0, float* p1, int k_begin, int k_end) {
   __shared__ float ys[128];
   __shared__ double red[8];
-  if (!mv.begin(blockIdx.x)) return;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  double d0 = 0.0, d1 = 0.0;
-  for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x) {
-    float acc[16];
+  mv.p.seq0 = up.p.seq0 = pc_seq_base(mv.p);  // the epoch is fixed for the whole solve
+#ifdef TSB_CG_TRACE
+  __shared__ unsigned cgt_slot;
+#endif
+  for (int k = k_begin; k <= k_end; ++k) {
+#ifdef TSB_CG_TRACE
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      cgt_slot = atomicAdd(&g_cg_trace_n, 1u) & 511u;
+      g_cg_trace[cgt_slot][0] = cgt_now();
+    }
+#endif
+    mv.k = up.k = k;
+    mv.pcur = (k & 1) ? p1 : p0;
+    up.pcur = mv.pcur;
+    mv.pprev = (k & 1) ? p0 : p1;
+    mv.beta = up.alpha = 0.f;
+    if (!mv.begin(blockIdx.x)) return;
+    CGT(1);
+    double d0 = 0.0;
+    for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x) {
+      float acc[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-    const int e = row_ptr[i + 1];
-    for (int idx = row_ptr[i]; idx < e; ++idx) {
-      const int64_t j = col_idx[idx];
-      const float4 xv = mv.x4(j * 128 + 4 * lane);
-      const float4* bp = blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
-      float4 a[16];
+      for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+      const int e = row_ptr[i + 1];
+      for (int idx = row_ptr[i]; idx < e; ++idx) {
+        const int64_t j = col_idx[idx];
+        const float4 xv = mv.x4(j * 128 + 4 * lane);
+        const float4* bp = blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
+        float4 a[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) a[r] = __ldcs(bp + r * 32);
+        for (int r = 0; r < 16; ++r) a[r] = KEEP ? __ldg(bp + r * 32) : __ldcs(bp + r * 32);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          acc[r] = fmaf(a[r].x, xv.x, acc[r]);
+          acc[r] = fmaf(a[r].y, xv.y, acc[r]);
+          acc[r] = fmaf(a[r].z, xv.z, acc[r]);
+          acc[r] = fmaf(a[r].w, xv.w, acc[r]);
+        }
+      }
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
-        acc[r] = fmaf(a[r].x, xv.x, acc[r]);
-        acc[r] = fmaf(a[r].y, xv.y, acc[r]);
-        acc[r] = fmaf(a[r].z, xv.z, acc[r]);
-        acc[r] = fmaf(a[r].w, xv.w, acc[r]);
+        const float v = warp_sum(acc[r]);
+        if (lane == r) ys[w * 16 + r] = v;
       }
+      __syncthreads();
+      double dd = 0.0;
+      if (threadIdx.x < 128) mv.row(static_cast<int64_t>(i) * 128 + threadIdx.x, ys[threadIdx.x], &d0, &dd);
+      __syncthreads();
     }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float v = warp_sum(acc[r]);
-      if (lane == r) ys[w * 16 + r] = v;
+    CGT(2);
+    {
+      const double t0 = block_sum256(d0, red);
+      if (threadIdx.x == 0) mv.finish(t0, 0.0);
     }
-    __syncthreads();
-    if (threadIdx.x < 128) mv.row(static_cast<int64_t>(i) * 128 + threadIdx.x, ys[threadIdx.x], &d0, &d1);
-    __syncthreads();
+    mv.tail();
+    CGT(3);
+    if (k >= mv.max_iter) return;
+    if (!up.begin(blockIdx.x)) return;
+    CGT(6);
+    double e0 = 0.0, e1 = 0.0;
+    for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x)
+      if (threadIdx.x < 128) up.elem(static_cast<int64_t>(i) * 128 + threadIdx.x, &e0, &e1);
+    const double t0 = block_sum256(e0, red);
+    const double t1 = block_sum256(e1, red);
+    if (threadIdx.x == 0) up.finish(t0, t1);
+    up.tail();
+    CGT(7);
   }
-  {
-    const double t0 = block_sum256(d0, red);
-    if (threadIdx.x == 0) mv.finish(t0, 0.0);
-  }
-  mv.tail();
-  if (mv.k >= mv.max_iter) return;
-  if (!up.begin(blockIdx.x)) return;
-  double e0 = 0.0, e1 = 0.0;
-  for (int i = blockIdx.x; i < n_block_rows; i += gridDim.x)
-    if (threadIdx.x < 128) up.elem(static_cast<int64_t>(i) * 128 + threadIdx.x, &e0, &e1);
-  const double t0 = block_sum256(e0, red);
-  const double t1 = block_sum256(e1, red);
-  if (threadIdx.x == 0) up.finish(t0, t1);
-  up.tail();
 }
 
 }  // namespace
 }  // namespace tsb
 
-extern "C" int trnsparse_bsr_cg_coop_iter(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
-                                          const int* col_idx, const float* blocks, float* x, const float* inv_d,
-                                          double tol, int max_iter, int k, void* ws, PEER_ARGS, void* stream) {
+extern "C" int trnsparse_bsr_cg_coop_run(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                         const int* col_idx, const float* blocks, float* x, const float* inv_d,
+                                         double tol, int max_iter, int k_begin, int k_end, void* ws, PEER_ARGS,
+                                         void* stream) {
   const BsrDesc d = BSR_DESC;
-  int rc = check_desc(d, "bsr_cg_coop_iter");
+  int rc = check_desc(d, "bsr_cg_coop_run");
   if (rc) return rc;
-  TSB_REQUIRE(ws && x && k >= 0 && k <= max_iter && peers && world > 0, "bsr_cg_coop_iter: bad argument");
-  TSB_REQUIRE(d.fast(), "bsr_cg_coop_iter: needs block size 128 and block-aligned shapes");
+  TSB_REQUIRE(ws && x && 0 <= k_begin && k_begin <= k_end && k_end <= max_iter && peers && world > 0,
+              "bsr_cg_coop_run: bad argument");
+  TSB_REQUIRE(d.fast(), "bsr_cg_coop_run: needs block size 128 and block-aligned shapes");
   cudaStream_t st = as_stream(stream);
   const CgWs w = cg_ws(ws, n, max_iter);
-  TSB_REQUIRE(all_aligned({inv_d, w.r, w.p0, w.p1, x}), "bsr_cg_coop_iter: vectors must be 16-byte aligned");
-  float* pcur = (k & 1) ? w.p1 : w.p0;
-  const float* pprev = (k & 1) ? w.p0 : w.p1;
-  CgMvFused mv{inv_d, w, pprev, pcur, k, max_iter, tol, m, PEER_CTX, 0.f};
-  CgUpdateFused up{inv_d, x, w, pcur, k, max_iter, PEER_CTX, 0.f};
+  TSB_REQUIRE(all_aligned({inv_d, w.r, w.p0, w.p1, x}), "bsr_cg_coop_run: vectors must be 16-byte aligned");
+  CgMvFused mv{inv_d, w, w.p1, w.p0, k_begin, max_iter, tol, m, PEER_CTX, 0.f};
+  CgUpdateFused up{inv_d, x, w, w.p0, k_begin, max_iter, PEER_CTX, 0.f};
+  const bool keep = fits_l2(static_cast<size_t>(n_blocks) * 128 * 128 * 4);
+  const void* kern = keep ? (const void*)cg_solve_coop_kernel<true> : (const void*)cg_solve_coop_kernel<false>;
   int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cg_iter_coop_kernel, 256, 0);
-  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_coop_iter: occupancy");
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_coop_run: occupancy");
   int64_t nbr = d.block_rows();
   int64_t grid = static_cast<int64_t>(sm_count()) * (per_sm < 1 ? 1 : per_sm);
   if (grid > nbr) grid = nbr;
   if (grid < 1) grid = 1;
   const float4* bl = reinterpret_cast<const float4*>(blocks);
   int nbr_i = (int)nbr;
-  void* args[] = {(void*)&row_ptr, (void*)&col_idx, (void*)&bl, (void*)&nbr_i, (void*)&mv, (void*)&up};
-  e = cudaLaunchCooperativeKernel((const void*)cg_iter_coop_kernel, dim3((unsigned)grid), dim3(256), args, 0, st);
-  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_coop_iter: cooperative launch");
+  float* p0 = w.p0;
+  float* p1 = w.p1;
+  void* args[] = {(void*)&row_ptr, (void*)&col_idx, (void*)&bl, (void*)&nbr_i, (void*)&mv,
+                  (void*)&up,      (void*)&p0,      (void*)&p1, (void*)&k_begin, (void*)&k_end};
+  e = cudaLaunchCooperativeKernel(kern, dim3((unsigned)grid), dim3(256), args, 0, st);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cg_coop_run: cooperative launch");
   return TRNSPARSE_OK;
 }
+
+// ---------------------------------------------------------------- sharded CG, one reduction per iteration
+// Chronopoulos & Gear's formulation of preconditioned CG ("s-step methods
+// and their parallel implementation", J. Comput. Appl. Math. 25, 1989): with
+// u = M r and w = A u carried along, the iteration's two inner-product rounds
+// of standard PCG become one, since p.Ap = delta - beta * gamma / alpha_prev
+// with gamma = r.u and delta = w.u; s = A p follows the recurrence
+// s = w + beta s. Per iteration k (gamma_k, delta_k, r_k.r_k known):
+//   beta = gamma_k / gamma_{k-1};  p.Ap = delta_k - beta gamma_k / alpha_{k-1}
+//   alpha = gamma_k / p.Ap
+//   p = u + beta p;  s = w + beta s;  x += alpha p;  r -= alpha s
+//   u = M r;  w = A u;  then gamma_{k+1}, delta_{k+1}, r.r in one reduction.
+// In exact arithmetic these are the reference's iterates (trnsparse/
+// iterative.py:53-126); the convergence test (||r|| / ||b|| after the update)
+// and the |p.Ap| < 1e-30 breakdown test sit where the reference has them.
+//
+// One cooperative launch runs the whole solve. The SpMV input u = M r of a
+// column is formed on the fly from the previous iteration's r, s and w (so
+// own and halo columns need no extra pass), the owner CTA of a row writes the
+// new r, s, p, x, w of that row, and the halo copies of r and s are written by
+// the CTAs that form them. r, s and w are double-buffered by iteration
+// parity. The exchange after the SpMV carries three partial sums and the new
+// w rows the neighbours hold as halo; every rank's buffers have the same
+// layout (n_alloc entries per vector), so halo destinations are element
+// offsets. The peer flags double as the grid-wide barrier.
+namespace tsb {
+namespace {
+
+struct CgcgWs {
+  SolverStatus* st;
+  Slot* slots;  // slot k: {a: p_k.Ap_k, b: gamma_k, c: delta_k, d: r_k.r_k}
+  float* r[2];
+  float* s[2];
+  float* w[2];
+  float* p;
+};
+constexpr int kCgcgVecs = 7;
+
+inline size_t cgcg_head(int max_iter) { return align256(64) + align256(sizeof(Slot) * (size_t)(max_iter + 2)); }
+inline size_t cgcg_ws_size(int64_t n, int max_iter) {
+  return cgcg_head(max_iter) + kCgcgVecs * align256(sizeof(float) * (size_t)n);
+}
+inline CgcgWs cgcg_ws(void* base, int64_t n, int max_iter) {
+  char* p = static_cast<char*>(base);
+  CgcgWs w;
+  w.st = reinterpret_cast<SolverStatus*>(p);
+  w.slots = reinterpret_cast<Slot*>(p + align256(64));
+  char* v = p + cgcg_head(max_iter);
+  const size_t vb = align256(sizeof(float) * (size_t)n);
+  for (int i = 0; i < 2; ++i) {
+    w.r[i] = reinterpret_cast<float*>(v + (0 + i) * vb);
+    w.s[i] = reinterpret_cast<float*>(v + (2 + i) * vb);
+    w.w[i] = reinterpret_cast<float*>(v + (4 + i) * vb);
+  }
+  w.p = reinterpret_cast<float*>(v + 6 * vb);
+  return w;
+}
+
+struct Cgcg {
+  const int* row_ptr;
+  const int* col_idx;
+  const float4* blocks;
+  int n_block_rows;
+  int64_t n_own;
+  const float* inv_d;  // n_alloc, halo filled; null = no preconditioner
+  const float* bvec;   // n_own
+  float* x;            // n_own
+  CgcgWs ws;
+  size_t ws_off;       // byte offset of the workspace inside every rank's peer buffer
+  size_t vec_bytes;
+  size_t head;
+  double tol;
+  int max_iter;
+  PeerCtx p;           // sends: (source element, destination rank, destination element)
+};
+
+__device__ __forceinline__ float cg_m(const float* inv_d, int64_t c, float r) {
+  return inv_d ? __fmul_rn(r, inv_d[c]) : r;
+}
+
+// Wait (bounded) until every rank's flag of `area` reached `seq`; return the
+// rank-ordered sums of the first three partials.
+__device__ double3 cgcg_wait(const PeerCtx& p, int area, long long seq) {
+  __shared__ double3 tot;
+  char* mine = p.peers[p.rank];
+  if (threadIdx.x < p.world) {
+    const long long* f = pc_flags(p, mine) + area * p.world + threadIdx.x;
+    uint32_t i = 0;
+    while (ld_acq_sys(f) < seq) {
+      if (++i > kSpinLimit) {
+        record_device_error(DEVERR_PEER_TIMEOUT);
+        break;
+      }
+      __nanosleep(20);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const volatile double* v = pc_vals(p, mine) + area * p.world * 4;
+    double a = 0.0, b = 0.0, c = 0.0;
+    for (int q = 0; q < p.world; ++q) {
+      a += v[4 * q];
+      b += v[4 * q + 1];
+      c += v[4 * q + 2];
+    }
+    tot = make_double3(a, b, c);
+  }
+  __syncthreads();
+  return tot;
+}
+
+// Last CTA (ticket counter `which`; one counter per kernel, whose grid size is
+// fixed) publishes the three local totals of `slot` and, when
+// `src` is set, the halo rows of that vector (at byte offset `vec_off` of the
+// workspace) to every rank, then raises the flags.
+__device__ void cgcg_publish(const Cgcg& g, int which, int area, long long seq, const Slot* slot, const float* src,
+                             size_t vec_off) {
+  __shared__ int last;
+  __shared__ double3 part;
+  const PeerCtx& p = g.p;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned t;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;\n" : "=r"(t) : "l"(pc_ticket(p, which)) : "memory");
+    last = ((t + 1) % gridDim.x) == 0;
+    if (last) {
+      const volatile double* v = &slot->b;
+      part = make_double3(v[0], v[1], v[2]);
+    }
+  }
+  __syncthreads();
+  if (!last) return;
+#ifdef TSB_CG_TRACE
+  if (threadIdx.x == 0) g_cg_trace[(g_cg_trace_n - 1) & 511u][4] = cgt_now();
+#endif
+  if (src) {
+    for (int q = 0; q < p.n_sends; ++q) {
+      const long long so = p.sends[3 * q], dr = p.sends[3 * q + 1], de = p.sends[3 * q + 2];
+      float4* dst = reinterpret_cast<float4*>(p.peers[dr] + g.ws_off + vec_off + 4 * de);
+      const volatile float4* sp = reinterpret_cast<const volatile float4*>(src + so);
+      for (int i = threadIdx.x; i < p.chunk / 4; i += blockDim.x) dst[i] = make_float4(sp[i].x, sp[i].y, sp[i].z, sp[i].w);
+    }
+  }
+  if (threadIdx.x < p.world) {
+    double* v = pc_vals(p, p.peers[threadIdx.x]) + (area * p.world + p.rank) * 4;
+    v[0] = part.x;
+    v[1] = part.y;
+    v[2] = part.z;
+  }
+  __syncthreads();  // the stores above happen-before each flag's release at system scope
+  if (threadIdx.x < p.world) st_rel_sys(pc_flags(p, p.peers[threadIdx.x]) + area * p.world + p.rank, seq);
+#ifdef TSB_CG_TRACE
+  if (threadIdx.x == 0) g_cg_trace[(g_cg_trace_n - 1) & 511u][5] = cgt_now();
+#endif
+}
+
+// SpMV of one block-row with the input column vector formed by `in(c)` (4
+// consecutive columns per lane); returns the row sums in ys[0..127].
+template <bool KEEP, class In>
+__device__ __forceinline__ void cgcg_row_mv(const Cgcg& g, int i, float* ys, In in) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float acc[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+  const int e = g.row_ptr[i + 1];
+  for (int idx = g.row_ptr[i]; idx < e; ++idx) {
+    const int64_t j = g.col_idx[idx];
+    const float4 xv = in(j * 128 + 4 * lane);
+    const float4* bp = g.blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
+    float4 a[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) a[r] = KEEP ? __ldg(bp + r * 32) : __ldcs(bp + r * 32);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      acc[r] = fmaf(a[r].x, xv.x, acc[r]);
+      acc[r] = fmaf(a[r].y, xv.y, acc[r]);
+      acc[r] = fmaf(a[r].z, xv.z, acc[r]);
+      acc[r] = fmaf(a[r].w, xv.w, acc[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    const float v = warp_sum(acc[r]);
+    if (lane == r) ys[w * 16 + r] = v;
+  }
+  __syncthreads();
+}
+
+// Block sum of three doubles; thread 0 adds them into slot->{b, c, d}.
+__device__ __forceinline__ void cgcg_add3(double a, double b, double c, double* red, Slot* slot) {
+  a = block_sum256(a, red);
+  b = block_sum256(b, red);
+  c = block_sum256(c, red);
+  if (threadIdx.x == 0) {
+    atomicAdd(&slot->b, a);
+    atomicAdd(&slot->c, b);
+    atomicAdd(&slot->d, c);
+  }
+}
+
+// exchange steps: 0 = setup (r0 halo, ||b||^2), 1 + k = (gamma, delta, r.r)_k and w_k halo
+template <bool KEEP>
+__global__ void __launch_bounds__(256, 2)
+cgcg_solve_kernel(Cgcg g) {
+  __shared__ float ys[128];
+  __shared__ double red[8];
+  SolverStatus* st = g.ws.st;
+  const long long seq0 = pc_seq_base(g.p);
+  g.p.seq0 = seq0;
+  const int64_t halo_begin = g.n_own;
+  const size_t w_off0 = g.head + 4 * g.vec_bytes, w_off1 = g.head + 5 * g.vec_bytes;
+
+  // ---- setup part 2: ||b||^2 and the r0 halo have arrived; w0 = A u0 with u0 = M r0
+  const double bb = cgcg_wait(g.p, 2, seq0 + 1).x;
+  if (bb < 1e-30) {  // ||b|| < 1e-15: x = 0 (reference: zero right-hand side)
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      st->bb = bb;
+      set_done(st, 0, REASON_ZERO_RHS, 0.0);
+    }
+    return;
+  }
+  {
+    const float* r0 = g.ws.r[0];
+    double ga = 0.0, de = 0.0, rr = 0.0;
+    for (int i = blockIdx.x; i < g.n_block_rows; i += gridDim.x) {
+      cgcg_row_mv<KEEP>(g, i, ys, [&](int64_t c) {
+        const float4 r = ld4(r0 + c);
+        return make_float4(cg_m(g.inv_d, c, r.x), cg_m(g.inv_d, c + 1, r.y), cg_m(g.inv_d, c + 2, r.z),
+                           cg_m(g.inv_d, c + 3, r.w));
+      });
+      if (threadIdx.x < 128) {
+        const int64_t row = static_cast<int64_t>(i) * 128 + threadIdx.x;
+        const float r = r0[row], u = cg_m(g.inv_d, row, r), wv = ys[threadIdx.x];
+        g.ws.w[0][row] = wv;
+        ga += (double)r * (double)u;
+        de += (double)wv * (double)u;
+        rr += (double)r * (double)r;
+      }
+      __syncthreads();
+    }
+    cgcg_add3(ga, de, rr, red, &g.ws.slots[0]);
+    cgcg_publish(g, 3, 0, seq0 + 2, &g.ws.slots[0], g.ws.w[0], w_off0);
+  }
+  double gam_prev = 0.0, alpha_prev = 0.0;
+#ifdef TSB_CG_TRACE
+  __shared__ unsigned cgt_slot;
+#endif
+  for (int k = 0;; ++k) {
+    const int cur = k & 1, nxt = cur ^ 1;
+#ifdef TSB_CG_TRACE
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      cgt_slot = atomicAdd(&g_cg_trace_n, 1u) & 511u;
+      g_cg_trace[cgt_slot][0] = cgt_now();
+    }
+#endif
+    const double3 t = cgcg_wait(g.p, k & 1, seq0 + 2 + k);
+    CGT(1);
+    const double gam = t.x, del = t.y, rr = t.z;
+    if (k > 0) {
+      const double rel = (double)(float)sqrt(rr) / sqrt(bb);
+      if (rel < g.tol) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) set_done(st, k, REASON_CONVERGED, rel);
+        return;
+      }
+    }
+    if (k >= g.max_iter) {
+      if (blockIdx.x == 0 && threadIdx.x == 0)
+        set_done(st, g.max_iter, REASON_MAXITER, k > 0 ? (double)(float)sqrt(rr) / sqrt(bb) : nan(""));
+      return;
+    }
+    const double beta_d = k > 0 ? gam / gam_prev : 0.0;
+    const double pap = k > 0 ? del - beta_d * gam / alpha_prev : del;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      if (k == 0) st->bb = bb;
+      g.ws.slots[k].a = pap;
+    }
+    if (fabs(pap) < 1e-30) {
+      if (blockIdx.x == 0 && threadIdx.x == 0)
+        set_done(st, g.max_iter, REASON_BREAKDOWN, k > 0 ? (double)(float)sqrt(rr) / sqrt(bb) : nan(""));
+      return;
+    }
+    const double alpha_d = gam / pap;
+    const float alpha = (float)alpha_d, beta = (float)beta_d;
+    gam_prev = gam;
+    alpha_prev = alpha_d;
+    const float *rc = g.ws.r[cur], *sc = g.ws.s[cur], *wc = g.ws.w[cur];
+    float *rn = g.ws.r[nxt], *sn = g.ws.s[nxt], *wn = g.ws.w[nxt];
+    // s_k = w_k + beta s_{k-1};  r_{k+1} = r_k - alpha s_k;  u_{k+1} = M r_{k+1}
+    auto form = [&](int64_t c, float* r_out, float* s_out) {
+      const float s = __fadd_rn(wc[c], __fmul_rn(beta, sc[c]));
+      const float r = __fsub_rn(rc[c], __fmul_rn(alpha, s));
+      *s_out = s;
+      *r_out = r;
+      return cg_m(g.inv_d, c, r);
+    };
+    double ga = 0.0, de = 0.0, rr_new = 0.0;
+    for (int i = blockIdx.x; i < g.n_block_rows; i += gridDim.x) {
+      cgcg_row_mv<KEEP>(g, i, ys, [&](int64_t c) {
+        // four consecutive columns: vector loads of w, s, r and the preconditioner
+        const float4 w4 = ld4(wc + c), s4 = ld4(sc + c), r4 = ld4(rc + c);
+        const float4 d4 = g.inv_d ? ld4(g.inv_d + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+        const float rv[4] = {r4.x, r4.y, r4.z, r4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+        float r[4], s[4], u[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          s[q] = __fadd_rn(wv[q], __fmul_rn(beta, sv[q]));
+          r[q] = __fsub_rn(rv[q], __fmul_rn(alpha, s[q]));
+          u[q] = g.inv_d ? __fmul_rn(r[q], dv[q]) : r[q];
+        }
+        if (c >= halo_begin) {  // halo copies: every CTA that needs them writes the same values
+          *reinterpret_cast<float4*>(rn + c) = make_float4(r[0], r[1], r[2], r[3]);
+          *reinterpret_cast<float4*>(sn + c) = make_float4(s[0], s[1], s[2], s[3]);
+        }
+        return make_float4(u[0], u[1], u[2], u[3]);
+      });
+      if (threadIdx.x < 128) {
+        const int64_t row = static_cast<int64_t>(i) * 128 + threadIdx.x;
+        float r, s;
+        const float u = form(row, &r, &s);
+        rn[row] = r;
+        sn[row] = s;
+        const float pk = __fadd_rn(cg_m(g.inv_d, row, rc[row]), __fmul_rn(beta, g.ws.p[row]));
+        g.ws.p[row] = pk;
+        g.x[row] = __fadd_rn(g.x[row], __fmul_rn(alpha, pk));
+        const float wv = ys[threadIdx.x];
+        wn[row] = wv;
+        ga += (double)r * (double)u;
+        de += (double)wv * (double)u;
+        rr_new += (double)r * (double)r;
+      }
+      __syncthreads();
+    }
+    CGT(2);
+    cgcg_add3(ga, de, rr_new, red, &g.ws.slots[k + 1]);
+    CGT(3);
+    cgcg_publish(g, 3, (k + 1) & 1, seq0 + 3 + k, &g.ws.slots[k + 1], wn, nxt ? w_off1 : w_off0);
+    CGT(6);
+  }
+}
+
+// Setup part 1 (ordinary launch): r0 = b (x0 = 0), ||b||^2, then the r0 halo
+// and the partial to every rank (exchange step 0, area 2).
+__global__ void __launch_bounds__(256) cgcg_start_kernel(Cgcg g) {
+  __shared__ double red[8];
+  double bb = 0.0;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < g.n_own;
+       i += static_cast<int64_t>(gridDim.x) * 256) {
+    const float v = g.bvec[i];
+    g.ws.r[0][i] = v;
+    g.x[i] = 0.f;
+    bb += (double)v * (double)v;
+  }
+  cgcg_add3(bb, 0.0, 0.0, red, &g.ws.slots[g.max_iter + 1]);
+  cgcg_publish(g, 0, 2, pc_seq_base(g.p) + 1, &g.ws.slots[g.max_iter + 1], g.ws.r[0], g.head);
+}
+
+__global__ void cgcg_bump_epoch(char* const* peers, int rank, size_t comm_off, int world) {
+  *reinterpret_cast<long long*>(peers[rank] + comm_off + 120 * world) += 1;
+}
+
+}  // namespace
+}  // namespace tsb
+
+extern "C" size_t trnsparse_bsr_cgcg_workspace_size(int64_t n_alloc, int max_iter) {
+  return cgcg_ws_size(n_alloc < 0 ? 0 : n_alloc, max_iter < 0 ? 0 : max_iter);
+}
+
+extern "C" int trnsparse_bsr_cgcg_layout(int64_t n_alloc, int max_iter, size_t* offsets) {
+  TSB_REQUIRE(offsets && n_alloc >= 0 && max_iter >= 0, "bsr_cgcg_layout: bad argument");
+  const size_t head = cgcg_head(max_iter), vb = align256(sizeof(float) * (size_t)n_alloc);
+  offsets[0] = 0;             // status record
+  offsets[1] = align256(64);  // Slot[max_iter + 2]: {p.Ap, gamma, delta, r.r}
+  for (int i = 0; i < kCgcgVecs; ++i) offsets[2 + i] = head + i * vb;  // r0 r1 s0 s1 w0 w1 p
+  return TRNSPARSE_OK;
+}
+
+extern "C" int trnsparse_bsr_cgcg_solve(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                        const int* col_idx, const float* blocks, const float* b_vec, float* x,
+                                        const float* inv_d, double tol, int max_iter, int64_t n_alloc, void* ws,
+                                        size_t ws_off, size_t ws_bytes, PEER_ARGS, void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_cgcg_solve");
+  if (rc) return rc;
+  TSB_REQUIRE(d.fast(), "bsr_cgcg_solve: needs block size 128 and block-aligned shapes");
+  TSB_REQUIRE(ws && x && b_vec && max_iter >= 0 && n_alloc >= n && peers && world > 0 && rank >= 0 &&
+                  rank < world && (n_sends == 0 || sends),
+              "bsr_cgcg_solve: bad argument");
+  TSB_REQUIRE(ws_bytes >= cgcg_ws_size(n_alloc, max_iter), "bsr_cgcg_solve: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  Cgcg g;
+  g.row_ptr = row_ptr;
+  g.col_idx = col_idx;
+  g.blocks = reinterpret_cast<const float4*>(blocks);
+  g.n_block_rows = (int)d.block_rows();
+  g.n_own = m;
+  g.inv_d = inv_d;
+  g.bvec = b_vec;
+  g.x = x;
+  g.ws = cgcg_ws(ws, n_alloc, max_iter);
+  g.ws_off = ws_off;
+  g.vec_bytes = align256(sizeof(float) * (size_t)n_alloc);
+  g.head = cgcg_head(max_iter);
+  g.tol = tol;
+  g.max_iter = max_iter;
+  g.p = PEER_CTX;
+  TSB_REQUIRE(all_aligned({inv_d, x, g.ws.r[0], g.ws.p}), "bsr_cgcg_solve: vectors must be 16-byte aligned");
+  // Clear status, slots, s_{-1} and p_{-1}. r and w are left alone: they are written before
+  // they are read, and a faster peer may already have pushed this solve's r0 halo rows.
+  cudaError_t e = cudaMemsetAsync(ws, 0, g.head, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(g.ws.s[0], 0, g.vec_bytes, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(g.ws.p, 0, g.vec_bytes, st);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cgcg_solve: clear");
+  cgcg_bump_epoch<<<1, 1, 0, st>>>(reinterpret_cast<char* const*>(peers), rank, comm_off, world);
+  TSB_CHECK_LAUNCH("bsr_cgcg_solve: epoch");
+  cgcg_start_kernel<<<vec_grid(m), 256, 0, st>>>(g);
+  TSB_CHECK_LAUNCH("bsr_cgcg_solve: start");
+  const bool keep = fits_l2(static_cast<size_t>(n_blocks) * 128 * 128 * 4);
+  const void* kern = keep ? (const void*)cgcg_solve_kernel<true> : (const void*)cgcg_solve_kernel<false>;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cgcg_solve: occupancy");
+  int64_t grid = static_cast<int64_t>(sm_count()) * (per_sm < 1 ? 1 : per_sm);
+  if (grid > g.n_block_rows) grid = g.n_block_rows;
+  if (grid < 1) grid = 1;
+  void* args[] = {(void*)&g};
+  e = cudaLaunchCooperativeKernel(kern, dim3((unsigned)grid), dim3(256), args, 0, st);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_cgcg_solve: cooperative launch");
+  return TRNSPARSE_OK;
+}
+
+#ifdef TSB_CG_TRACE
+__device__ unsigned long long tsb::g_cg_trace[512][8];
+__device__ unsigned tsb::g_cg_trace_n;
+extern "C" __attribute__((visibility("default"))) int trnsparse_cg_trace_read(unsigned long long* host) {
+  unsigned zero = 0;
+  int rc = (int)cudaMemcpyFromSymbol(host, tsb::g_cg_trace, sizeof(tsb::g_cg_trace));
+  cudaMemcpyToSymbol(tsb::g_cg_trace_n, &zero, sizeof(zero));
+  return rc;
+}
+#endif

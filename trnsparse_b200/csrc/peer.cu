@@ -7,8 +7,9 @@
 // rank's solver workspace (so halo rows are written directly into the
 // receiver's vectors) followed by a small exchange area:
 //   flags[3][world]      int64, written by rank q into slot [area][q]
-//   vals[3][world][2]    float64 partial sums, same indexing
+//   vals[3][world][4]    float64 partial sums, same indexing (up to four per exchange)
 //   epoch                int64, bumped once per solve on every rank
+//   tickets[4]           uint32 CTA arrival counters of the solver kernels
 // trnsparse_peer_reduce_push replaces "all-reduce two doubles + halo
 // exchange" with one single-CTA kernel: push halo rows and the local partials
 // to every peer, fence, raise this rank's flag on every peer, wait (bounded)
@@ -39,7 +40,7 @@ __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
 
 struct CommArea {
   long long* flags;  // [3][world]
-  double* vals;      // [3][world][2]
+  double* vals;      // [3][world][4]
   long long* epoch;
 };
 
@@ -47,7 +48,7 @@ __device__ __forceinline__ CommArea area_of(char* base, size_t comm_off, int wor
   CommArea a;
   a.flags = reinterpret_cast<long long*>(base + comm_off);
   a.vals = reinterpret_cast<double*>(base + comm_off + 24 * world);
-  a.epoch = reinterpret_cast<long long*>(base + comm_off + 72 * world);
+  a.epoch = reinterpret_cast<long long*>(base + comm_off + 120 * world);
   return a;
 }
 
@@ -73,11 +74,11 @@ reduce_push_kernel(char* const* __restrict__ peers, int world, int rank, size_t 
   // 2. local partials into every rank's vals[area][rank]
   if (threadIdx.x < world) {
     const CommArea pq = area_of(peers[threadIdx.x], comm_off, world);
-    double* v = pq.vals + (static_cast<size_t>(area) * world + rank) * 2;
+    double* v = pq.vals + (static_cast<size_t>(area) * world + rank) * 4;
     v[0] = my_a ? *my_a : 0.0;
     v[1] = my_b ? *my_b : 0.0;
   }
-  __threadfence_system();
+  // the stores above happen-before (barrier) each flag's release at system scope
   __syncthreads();
   // 3. raise this rank's flag on every peer
   if (threadIdx.x < world) {
@@ -102,7 +103,7 @@ reduce_push_kernel(char* const* __restrict__ peers, int world, int rank, size_t 
     __threadfence_system();
     double ta = 0.0, tb = 0.0;
     for (int q = 0; q < world; ++q) {
-      const volatile double* v = me.vals + (static_cast<size_t>(area) * world + q) * 2;
+      const volatile double* v = me.vals + (static_cast<size_t>(area) * world + q) * 4;
       ta += v[0];
       tb += v[1];
     }
@@ -121,7 +122,7 @@ __global__ void bump_epoch_kernel(char* mine, size_t comm_off, int world) {
 
 using namespace tsb;
 
-extern "C" size_t trnsparse_peer_comm_bytes(int world) { return static_cast<size_t>(72 * world + 64); }
+extern "C" size_t trnsparse_peer_comm_bytes(int world) { return static_cast<size_t>(120 * world + 64); }
 
 extern "C" int trnsparse_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
   TSB_REQUIRE(bytes > 0 && ptr && ipc_handle, "peer_alloc: bad argument");

@@ -149,6 +149,9 @@ class _RawDevice:
         self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
 
 
+PEER_TRANSPORTS = ("peer", "fused", "coop", "cgcg")
+
+
 class ShardedCG:
     """A prepared sharded Jacobi-PCG solve for one shard, right-hand side and
     iteration budget.
@@ -156,7 +159,11 @@ class ShardedCG:
     transport="nccl": scalar all-reduces and halo exchanges are NCCL
     collectives / send-recv. transport="fused": the exchanges happen inside
     the two solver kernels of an iteration (see trnsparse_bsr_cg_fused_*);
-    transport="coop": the same in one cooperative kernel per iteration.
+    transport="coop": the same in one cooperative kernel for the whole solve
+    (the peer flags double as the grid barrier between phases).
+    transport="cgcg": one cooperative kernel for the whole solve with one
+    exchange per iteration (Chronopoulos-Gear recurrences: the reference's
+    iterates in exact arithmetic, half the synchronisations).
     transport="peer": the workspace lives in a CUDA
     IPC buffer every rank maps, and one single-CTA kernel per exchange pushes
     the halo rows and partial sums straight into the peers' memory over
@@ -194,21 +201,32 @@ class ShardedCG:
             halo_exchange(shard, self.inv_d, group)
         self.b = b_local.to(dev, torch.float32).contiguous()
         self.x = torch.zeros(n_own, dtype=torch.float32, device=dev)
-        self.ws_bytes = _lib.raw("trnsparse_bsr_cg_workspace_size")(n_ext, max_iter)
         self.transport = transport
         self._peer_ptrs: list[int] = []
-        if transport in ("peer", "fused", "coop"):
+        if transport == "cgcg":
+            # one layout on every rank: vectors sized for the largest extended shard
+            sizes = [None] * dist.get_world_size(group)
+            dist.all_gather_object(sizes, n_ext, group=group)
+            self.n_alloc = max(sizes)
+            self.ws_bytes = _lib.raw("trnsparse_bsr_cgcg_workspace_size")(self.n_alloc, max_iter)
+        else:
+            self.ws_bytes = _lib.raw("trnsparse_bsr_cg_workspace_size")(n_ext, max_iter)
+        if transport in PEER_TRANSPORTS:
             self._setup_peer(max_iter)
         elif transport == "nccl":
             self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
         else:
-            raise ValueError(f"transport must be 'nccl', 'peer', 'fused' or 'coop', got {transport!r}")
-        offs = (ctypes.c_size_t * 6)()
-        _lib.call("trnsparse_bsr_cg_layout", n_ext, max_iter, offs)
+            raise ValueError(f"transport must be one of 'nccl', {', '.join(map(repr, PEER_TRANSPORTS))}; "
+                             f"got {transport!r}")
+        offs = (ctypes.c_size_t * 9)()
+        if transport == "cgcg":
+            _lib.call("trnsparse_bsr_cgcg_layout", self.n_alloc, max_iter, offs)
+        else:
+            _lib.call("trnsparse_bsr_cg_layout", n_ext, max_iter, offs)
         self.offs = list(offs)
         self.r_vec = self.ws[offs[2] : offs[2] + 4 * n_ext].view(torch.float32)
-        if transport in ("peer", "fused", "coop"):
-            self._build_sends()
+        if transport in PEER_TRANSPORTS:
+            self._build_sends(element_offsets=transport == "cgcg")
         self.graph = None
         if graph:
             if self.tol > 0:
@@ -256,9 +274,11 @@ class ShardedCG:
         self.peers_dev = torch.tensor(ptrs, dtype=torch.int64, device=self.dev)
         self.ws = torch.as_tensor(_RawDevice(self._own_ptr, total), device=self.dev)[: self.ws_bytes]
 
-    def _build_sends(self) -> None:
+    def _build_sends(self, element_offsets: bool = False) -> None:
+        """Halo rows this rank pushes: (source element, destination rank, destination byte offset
+        of the receiver's r) or, with ``element_offsets``, the destination element."""
         sh = self.shard
-        info = (sh.n_own, self.offs[2], dict(sh.recv_from))
+        info = (sh.n_own, 0 if element_offsets else self.offs[2], dict(sh.recv_from))
         infos = [None] * self.world
         dist.all_gather_object(infos, info, group=self.group)
         b = sh.block_size
@@ -268,7 +288,8 @@ class ShardedCG:
             start, count = recv_q[self.rank]
             assert count == len(rows)
             for i, row in enumerate(rows):
-                sends.append((row * b, q, r_off_q + 4 * (n_own_q + (start + i) * b)))
+                dst = n_own_q + (start + i) * b
+                sends.append((row * b, q, dst if element_offsets else r_off_q + 4 * dst))
         self.n_sends = len(sends)
         self.sends_dev = torch.tensor(sends if sends else [(0, 0, 0)], dtype=torch.int64, device=self.dev)
 
@@ -282,7 +303,7 @@ class ShardedCG:
 
     def close(self) -> None:
         """Release the peer mappings and the shared buffer (peer transport)."""
-        if self.transport not in ("peer", "fused", "coop") or not hasattr(self, "_own_ptr"):
+        if self.transport not in PEER_TRANSPORTS or not hasattr(self, "_own_ptr"):
             return
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
@@ -300,6 +321,8 @@ class ShardedCG:
             return self._solve_peer()
         if self.transport in ("fused", "coop"):
             return self._solve_fused(coop=self.transport == "coop")
+        if self.transport == "cgcg":
+            return self._solve_cgcg()
         lib, sh, ws, offs, g = self._lib, self.shard, self.ws, self.offs, self.group
         s = lib.stream_handle(self.dev)
         n_own, n_ext = sh.n_own, sh.n_ext
@@ -352,17 +375,24 @@ class ShardedCG:
         self.x.zero_()
         lib.call("trnsparse_bsr_cg_fused_start", sh.n_own, sh.n_ext, sh.block_size, self.b.data_ptr(), inv,
                  self.max_iter, ws.data_ptr(), self.ws_bytes, *peer, s)
+        if coop:
+            lib.call("trnsparse_bsr_cg_coop_run", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, 0,
+                     self.max_iter, ws.data_ptr(), *peer, s)
+            return
         for k in range(self.max_iter + 1):
-            if coop:
-                lib.call("trnsparse_bsr_cg_coop_iter", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k,
-                         ws.data_ptr(), *peer, s)
-                continue
             lib.call("trnsparse_bsr_cg_fused_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 0,
                      ws.data_ptr(), *peer, s)
             if k == self.max_iter:
                 break
             lib.call("trnsparse_bsr_cg_fused_phase", *self.geo, self.x.data_ptr(), inv, self.tol, self.max_iter, k, 1,
                      ws.data_ptr(), *peer, s)
+
+    def _solve_cgcg(self) -> None:
+        lib, sh = self._lib, self.shard
+        lib.call("trnsparse_bsr_cgcg_solve", *self.geo, self.b.data_ptr(), self.x.data_ptr(), lib.ptr(self.inv_d),
+                 self.tol, self.max_iter, self.n_alloc, self.ws.data_ptr(), 0, self.ws_bytes,
+                 self.peers_dev.data_ptr(), self.world, self.rank, self.comm_off, self.sends_dev.data_ptr(),
+                 self.n_sends, lib.stream_handle(self.dev))
 
     def run(self) -> tuple[torch.Tensor, int, float]:
         with torch.cuda.device(self.dev):
