@@ -72,3 +72,39 @@ def test_sharded_cg(transport, world):
         err, it, itr, rel, relr = out[ci]
         assert err <= 1e-5, out[ci]
         assert abs(it - itr) <= 1, out[ci]
+
+
+def test_cgcg_peer_timeout_is_reported():
+    """A rank whose peer never answers: one process runs the one-reduction solver as
+    rank 0 of a world of 2 whose "peer" buffer is its own, so rank 1's flags are never
+    raised. The bounded wait gives up (10 s), the solve ends with the peer-timeout
+    status and the device error word says why; no GPU fault, the context stays usable."""
+    import ctypes
+
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import _lib
+    from trnsparse_b200 import workloads as w
+    from trnsparse_b200.ops import _bsr_geometry
+
+    dev = torch.device("cuda", 0)
+    A, b = w.block_pentadiagonal_spd(8)
+    n = A.shape[0]
+    geo = _bsr_geometry(A, dev)
+    ws_bytes = _lib.raw("trnsparse_bsr_cgcg_workspace_size")(n, 5)
+    comm_off = (ws_bytes + 255) // 256 * 256
+    buf = torch.zeros(comm_off + _lib.raw("trnsparse_peer_comm_bytes")(2), dtype=torch.uint8, device=dev)
+    peers = torch.tensor([buf.data_ptr(), buf.data_ptr()], dtype=torch.int64, device=dev)
+    sends = torch.zeros(3, dtype=torch.int64, device=dev)
+    x = torch.zeros(n, device=dev)
+    bd = b.to(dev)
+    _lib.device_error()  # start clean
+    _lib.call("trnsparse_bsr_cgcg_solve", *geo, bd.data_ptr(), x.data_ptr(), None, 0.0, 5, n, buf.data_ptr(), 0,
+              ws_bytes, peers.data_ptr(), 2, 0, comm_off, sends.data_ptr(), 0, _lib.stream_handle(dev))
+    torch.cuda.synchronize()
+    head = buf[:64].cpu()
+    assert head[0:4].view(torch.int32).item() == 1  # done
+    assert head[8:12].view(torch.int32).item() == 5  # REASON_PEER_TIMEOUT
+    assert _lib.device_error() == 3  # DEVERR_PEER_TIMEOUT (read and cleared)
+    # the context is still usable
+    y = ts.bsr_spmm(A, bd.unsqueeze(1))
+    assert torch.isfinite(y).all()

@@ -61,6 +61,7 @@ __device__ __forceinline__ void run_tail(const Op& op) {
 // stamps entry, after begin(), before finish() and after the tail.
 extern __device__ unsigned long long g_cg_trace[512][8];
 extern __device__ unsigned g_cg_trace_n;
+extern __device__ unsigned long long g_cg_cta[512][4];  // per-CTA stamps of one iteration
 __device__ __forceinline__ unsigned long long cgt_now() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -17,7 +17,14 @@
 namespace tsb {
 namespace {
 
-enum { REASON_NONE = 0, REASON_CONVERGED = 1, REASON_MAXITER = 2, REASON_BREAKDOWN = 3, REASON_ZERO_RHS = 4 };
+enum {
+  REASON_NONE = 0,
+  REASON_CONVERGED = 1,
+  REASON_MAXITER = 2,
+  REASON_BREAKDOWN = 3,
+  REASON_ZERO_RHS = 4,
+  REASON_PEER_TIMEOUT = 5,  // a sharded solve's exchange with a peer timed out
+};
 
 // First 64 bytes of every solver workspace (layout mirrored in Python).
 struct SolverStatus {
@@ -708,33 +715,30 @@ __device__ __forceinline__ long long pc_seq(const PeerCtx& p, long long step) {
   return (p.seq0 >= 0 ? p.seq0 : pc_seq_base(p)) + step + 1;
 }
 
-__device__ __forceinline__ long long ld_acq_sys(const long long* q) {
-  long long v;
-  asm volatile("ld.acquire.sys.global.s64 %0, [%1];\n" : "=l"(v) : "l"(q) : "memory");
-  return v;
-}
 __device__ __forceinline__ void st_rel_sys(long long* q, long long v) {
   asm volatile("st.release.sys.global.s64 [%0], %1;\n" ::"l"(q), "l"(v) : "memory");
 }
 
 // All threads of the CTA: wait for every rank's flag of `area` to reach the
 // step's sequence number, then return the rank-ordered sums of its partials.
+__device__ __forceinline__ bool peer_failed() { return *(volatile int*)&g_device_error == DEVERR_PEER_TIMEOUT; }
+
+// A wait that timed out (or follows one: the error word is sticky) yields NaN
+// totals; the callers see peer_failed() and end the solve as failed.
 __device__ double2 pc_wait_sum(const PeerCtx& p, int area, long long step) {
   __shared__ double2 tot;
+  __shared__ int fail;
   char* mine = p.peers[p.rank];
   const long long seq = pc_seq(p, step);
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
   if (threadIdx.x < p.world) {
-    const long long* f = pc_flags(p, mine) + area * p.world + threadIdx.x;
-    uint32_t i = 0;
-    while (ld_acq_sys(f) < seq) {
-      if (++i > kSpinLimit) {
-        record_device_error(DEVERR_PEER_TIMEOUT);
-        break;
-      }
-      __nanosleep(32);
-    }
+    const bool ok = *(volatile int*)&g_device_error != DEVERR_PEER_TIMEOUT &&
+                    wait_flag_geq(pc_flags(p, mine) + area * p.world + threadIdx.x, seq, 32);
+    if (!ok) fail = 1;
   }
   __syncthreads();
+  if (fail) return make_double2(nan(""), nan(""));
   if (threadIdx.x == 0) {
     const volatile double* v = pc_vals(p, mine) + area * p.world * 4;
     double a = 0.0, b = 0.0;
@@ -829,6 +833,10 @@ struct CgMvFused {
     SolverStatus* st = w.st;
     if (*(volatile int*)&st->done) return false;
     const double2 t = k == 0 ? pc_wait_sum(p, 2, 0) : pc_wait_sum(p, 1, 2 + 2 * (k - 1));
+    if (peer_failed()) {
+      if (cta == 0 && threadIdx.x == 0) set_done(st, k, REASON_PEER_TIMEOUT, nan(""));
+      return false;
+    }
     if (k == 0) {
       const double bnorm = sqrt(t.x);
       if (cta == 0 && threadIdx.x == 0) {
@@ -897,6 +905,10 @@ struct CgUpdateFused {
     SolverStatus* st = w.st;
     if (*(volatile int*)&st->done) return false;
     const double2 t = pc_wait_sum(p, 0, 1 + 2 * k);
+    if (peer_failed()) {
+      if (cta == 0 && threadIdx.x == 0) set_done(st, k, REASON_PEER_TIMEOUT, nan(""));
+      return false;
+    }
     const double pap = t.x;
     if (cta == 0 && threadIdx.x == 0) w.slots[k].a = pap;
     if (fabs(pap) < 1e-30) {
@@ -1187,21 +1199,20 @@ __device__ __forceinline__ float cg_m(const float* inv_d, int64_t c, float r) {
 
 // Wait (bounded) until every rank's flag of `area` reached `seq`; return the
 // rank-ordered sums of the first three partials.
+// A timed-out wait yields NaN totals (the caller ends the solve).
 __device__ double3 cgcg_wait(const PeerCtx& p, int area, long long seq) {
   __shared__ double3 tot;
+  __shared__ int fail;
   char* mine = p.peers[p.rank];
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
   if (threadIdx.x < p.world) {
-    const long long* f = pc_flags(p, mine) + area * p.world + threadIdx.x;
-    uint32_t i = 0;
-    while (ld_acq_sys(f) < seq) {
-      if (++i > kSpinLimit) {
-        record_device_error(DEVERR_PEER_TIMEOUT);
-        break;
-      }
-      __nanosleep(20);
-    }
+    const bool ok = *(volatile int*)&g_device_error != DEVERR_PEER_TIMEOUT &&
+                    wait_flag_geq(pc_flags(p, mine) + area * p.world + threadIdx.x, seq, 20);
+    if (!ok) fail = 1;
   }
   __syncthreads();
+  if (fail) return make_double3(nan(""), nan(""), nan(""));
   if (threadIdx.x == 0) {
     const volatile double* v = pc_vals(p, mine) + area * p.world * 4;
     double a = 0.0, b = 0.0, c = 0.0;
@@ -1261,22 +1272,36 @@ __device__ void cgcg_publish(const Cgcg& g, int which, int area, long long seq, 
 #endif
 }
 
-// SpMV of one block-row with the input column vector formed by `in(c)` (4
-// consecutive columns per lane); returns the row sums in ys[0..127].
-template <bool KEEP, class In>
-__device__ __forceinline__ void cgcg_row_mv(const Cgcg& g, int i, float* ys, In in) {
+// Inputs of four consecutive columns of the on-the-fly SpMV operand.
+struct Col4 {
+  float4 w, s, r, d;
+};
+
+// SpMV of one block-row; the input of four consecutive columns (per lane) is
+// fetched by `fetch(c)` and formed by `make(c, fetched)`. Per block the
+// input's loads go out first, then the block's, then the input is formed
+// (its halo stores may alias the blocks as far as the compiler knows, so they
+// come after every load); the next column index is fetched ahead. Returns
+// the row sums in ys[0..127].
+template <bool KEEP, class Fetch, class Make>
+__device__ __forceinline__ void cgcg_row_mv(const Cgcg& g, int i, float* ys, Fetch fetch, Make make) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   float acc[16];
 #pragma unroll
   for (int r = 0; r < 16; ++r) acc[r] = 0.f;
   const int e = g.row_ptr[i + 1];
-  for (int idx = g.row_ptr[i]; idx < e; ++idx) {
-    const int64_t j = g.col_idx[idx];
-    const float4 xv = in(j * 128 + 4 * lane);
+  int idx = g.row_ptr[i];
+  int64_t j = idx < e ? g.col_idx[idx] : 0;
+  for (; idx < e; ++idx) {
+    const int64_t jn = idx + 1 < e ? g.col_idx[idx + 1] : 0;
+    const int64_t c = j * 128 + 4 * lane;
+    const Col4 in = fetch(c);
     const float4* bp = g.blocks + static_cast<int64_t>(idx) * 4096 + (w * 16) * 32 + lane;
     float4 a[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) a[r] = KEEP ? __ldg(bp + r * 32) : __ldcs(bp + r * 32);
+    const float4 xv = make(c, in);
+    j = jn;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       acc[r] = fmaf(a[r].x, xv.x, acc[r]);
@@ -1312,13 +1337,16 @@ cgcg_solve_kernel(Cgcg g) {
   __shared__ float ys[128];
   __shared__ double red[8];
   SolverStatus* st = g.ws.st;
-  const long long seq0 = pc_seq_base(g.p);
-  g.p.seq0 = seq0;
+  const long long seq0 = pc_seq_base(g.p);  // the epoch is fixed for the whole solve
   const int64_t halo_begin = g.n_own;
   const size_t w_off0 = g.head + 4 * g.vec_bytes, w_off1 = g.head + 5 * g.vec_bytes;
 
   // ---- setup part 2: ||b||^2 and the r0 halo have arrived; w0 = A u0 with u0 = M r0
   const double bb = cgcg_wait(g.p, 2, seq0 + 1).x;
+  if (peer_failed()) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) set_done(st, 0, REASON_PEER_TIMEOUT, nan(""));
+    return;
+  }
   if (bb < 1e-30) {  // ||b|| < 1e-15: x = 0 (reference: zero right-hand side)
     if (blockIdx.x == 0 && threadIdx.x == 0) {
       st->bb = bb;
@@ -1330,11 +1358,19 @@ cgcg_solve_kernel(Cgcg g) {
     const float* r0 = g.ws.r[0];
     double ga = 0.0, de = 0.0, rr = 0.0;
     for (int i = blockIdx.x; i < g.n_block_rows; i += gridDim.x) {
-      cgcg_row_mv<KEEP>(g, i, ys, [&](int64_t c) {
-        const float4 r = ld4(r0 + c);
-        return make_float4(cg_m(g.inv_d, c, r.x), cg_m(g.inv_d, c + 1, r.y), cg_m(g.inv_d, c + 2, r.z),
-                           cg_m(g.inv_d, c + 3, r.w));
-      });
+      cgcg_row_mv<KEEP>(
+          g, i, ys,
+          [&](int64_t c) {
+            Col4 v;
+            v.r = ld4(r0 + c);
+            v.d = g.inv_d ? ld4(g.inv_d + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+            return v;
+          },
+          [&](int64_t, const Col4& v) {
+            return g.inv_d ? make_float4(__fmul_rn(v.r.x, v.d.x), __fmul_rn(v.r.y, v.d.y), __fmul_rn(v.r.z, v.d.z),
+                                         __fmul_rn(v.r.w, v.d.w))
+                           : v.r;
+          });
       if (threadIdx.x < 128) {
         const int64_t row = static_cast<int64_t>(i) * 128 + threadIdx.x;
         const float r = r0[row], u = cg_m(g.inv_d, row, r), wv = ys[threadIdx.x];
@@ -1362,6 +1398,13 @@ cgcg_solve_kernel(Cgcg g) {
 #endif
     const double3 t = cgcg_wait(g.p, k & 1, seq0 + 2 + k);
     CGT(1);
+    if (peer_failed()) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) set_done(st, k, REASON_PEER_TIMEOUT, nan(""));
+      return;
+    }
+#ifdef TSB_CG_TRACE
+    if (k == 10 && threadIdx.x == 0 && blockIdx.x < 512) g_cg_cta[blockIdx.x][2] = cgt_now();
+#endif
     const double gam = t.x, del = t.y, rr = t.z;
     if (k > 0) {
       const double rel = (double)(float)sqrt(rr) / sqrt(bb);
@@ -1402,25 +1445,32 @@ cgcg_solve_kernel(Cgcg g) {
     };
     double ga = 0.0, de = 0.0, rr_new = 0.0;
     for (int i = blockIdx.x; i < g.n_block_rows; i += gridDim.x) {
-      cgcg_row_mv<KEEP>(g, i, ys, [&](int64_t c) {
-        // four consecutive columns: vector loads of w, s, r and the preconditioner
-        const float4 w4 = ld4(wc + c), s4 = ld4(sc + c), r4 = ld4(rc + c);
-        const float4 d4 = g.inv_d ? ld4(g.inv_d + c) : make_float4(1.f, 1.f, 1.f, 1.f);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-        const float rv[4] = {r4.x, r4.y, r4.z, r4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
-        float r[4], s[4], u[4];
+      cgcg_row_mv<KEEP>(
+          g, i, ys,
+          [&](int64_t c) {
+            Col4 v;
+            v.w = ld4(wc + c);
+            v.s = ld4(sc + c);
+            v.r = ld4(rc + c);
+            v.d = g.inv_d ? ld4(g.inv_d + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+            return v;
+          },
+          [&](int64_t c, const Col4& v) {
+            const float wv[4] = {v.w.x, v.w.y, v.w.z, v.w.w}, sv[4] = {v.s.x, v.s.y, v.s.z, v.s.w};
+            const float rv[4] = {v.r.x, v.r.y, v.r.z, v.r.w}, dv[4] = {v.d.x, v.d.y, v.d.z, v.d.w};
+            float r[4], s[4], u[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          s[q] = __fadd_rn(wv[q], __fmul_rn(beta, sv[q]));
-          r[q] = __fsub_rn(rv[q], __fmul_rn(alpha, s[q]));
-          u[q] = g.inv_d ? __fmul_rn(r[q], dv[q]) : r[q];
-        }
-        if (c >= halo_begin) {  // halo copies: every CTA that needs them writes the same values
-          *reinterpret_cast<float4*>(rn + c) = make_float4(r[0], r[1], r[2], r[3]);
-          *reinterpret_cast<float4*>(sn + c) = make_float4(s[0], s[1], s[2], s[3]);
-        }
-        return make_float4(u[0], u[1], u[2], u[3]);
-      });
+            for (int q = 0; q < 4; ++q) {
+              s[q] = __fadd_rn(wv[q], __fmul_rn(beta, sv[q]));
+              r[q] = __fsub_rn(rv[q], __fmul_rn(alpha, s[q]));
+              u[q] = g.inv_d ? __fmul_rn(r[q], dv[q]) : r[q];
+            }
+            if (c >= halo_begin) {  // halo copies: every CTA that needs them writes the same values
+              *reinterpret_cast<float4*>(rn + c) = make_float4(r[0], r[1], r[2], r[3]);
+              *reinterpret_cast<float4*>(sn + c) = make_float4(s[0], s[1], s[2], s[3]);
+            }
+            return make_float4(u[0], u[1], u[2], u[3]);
+          });
       if (threadIdx.x < 128) {
         const int64_t row = static_cast<int64_t>(i) * 128 + threadIdx.x;
         float r, s;
@@ -1439,6 +1489,14 @@ cgcg_solve_kernel(Cgcg g) {
       __syncthreads();
     }
     CGT(2);
+#ifdef TSB_CG_TRACE
+    if (k == 10 && threadIdx.x == 0 && blockIdx.x < 512) {
+      g_cg_cta[blockIdx.x][0] = cgt_now();
+      unsigned smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      g_cg_cta[blockIdx.x][1] = smid;
+    }
+#endif
     cgcg_add3(ga, de, rr_new, red, &g.ws.slots[k + 1]);
     CGT(3);
     cgcg_publish(g, 3, (k + 1) & 1, seq0 + 3 + k, &g.ws.slots[k + 1], wn, nxt ? w_off1 : w_off0);
@@ -1539,6 +1597,10 @@ extern "C" int trnsparse_bsr_cgcg_solve(int64_t m, int64_t n, int b, int64_t n_b
 #ifdef TSB_CG_TRACE
 __device__ unsigned long long tsb::g_cg_trace[512][8];
 __device__ unsigned tsb::g_cg_trace_n;
+__device__ unsigned long long tsb::g_cg_cta[512][4];
+extern "C" __attribute__((visibility("default"))) int trnsparse_cg_cta_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, tsb::g_cg_cta, sizeof(tsb::g_cg_cta));
+}
 extern "C" __attribute__((visibility("default"))) int trnsparse_cg_trace_read(unsigned long long* host) {
   unsigned zero = 0;
   int rc = (int)cudaMemcpyFromSymbol(host, tsb::g_cg_trace, sizeof(tsb::g_cg_trace));

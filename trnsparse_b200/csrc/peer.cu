@@ -32,11 +32,6 @@ namespace {
 __device__ __forceinline__ void st_release_sys(long long* p, long long v) {
   asm volatile("st.release.sys.global.s64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
-  long long v;
-  asm volatile("ld.acquire.sys.global.s64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 struct CommArea {
   long long* flags;  // [3][world]
@@ -86,17 +81,9 @@ reduce_push_kernel(char* const* __restrict__ peers, int world, int rank, size_t 
     st_release_sys(pq.flags + static_cast<size_t>(area) * world + rank, seq);
   }
   // 4. wait for every peer's flag in this rank's area (bounded)
-  if (threadIdx.x < world) {
-    const long long* f = me.flags + static_cast<size_t>(area) * world + threadIdx.x;
-    uint32_t i = 0;
-    while (ld_acquire_sys(f) < seq) {
-      if (++i > kSpinLimit) {
-        record_device_error(DEVERR_PEER_TIMEOUT);
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
+  // bounded; once any exchange has timed out, later ones do not wait again
+  if (threadIdx.x < world && *(volatile int*)&g_device_error != DEVERR_PEER_TIMEOUT)
+    wait_flag_geq(me.flags + static_cast<size_t>(area) * world + threadIdx.x, seq, 64);
   __syncthreads();
   // 5. totals in rank order (identical on every rank)
   if (threadIdx.x == 0) {

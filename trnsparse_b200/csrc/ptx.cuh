@@ -87,6 +87,30 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Cross-GPU flags (the sharded solvers): wait, bounded by kPeerWaitNs of global
+// time, until *f >= seq (acquire at system scope). A peer may launch its side
+// late, hence the longer limit; on timeout the error word records
+// DEVERR_PEER_TIMEOUT and the caller winds the solve down.
+constexpr uint64_t kPeerWaitNs = 10000000000ull;  // 10 s
+
+__device__ __forceinline__ long long ld_acquire_sys_s64(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool wait_flag_geq(const long long* f, long long seq, unsigned sleep_ns) {
+  if (ld_acquire_sys_s64(f) >= seq) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (ld_acquire_sys_s64(f) >= seq) return true;
+    if ((i & 15u) == 0 && global_ns() - t0 > kPeerWaitNs) break;
+  }
+  record_device_error(DEVERR_PEER_TIMEOUT);
+  return false;
+}
+
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;

@@ -401,6 +401,8 @@ class ShardedCG:
             else:
                 self._solve(check=True)
         head = self.ws[:64].cpu()
+        if head[8:12].view(torch.int32).item() == 5:
+            raise RuntimeError("sharded CG: an exchange with a peer timed out (device error word set)")
         return self.x, head[4:8].view(torch.int32).item(), head[16:24].view(torch.float64).item()
 
     def executed_iterations(self) -> int:
