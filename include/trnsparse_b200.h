@@ -133,6 +133,28 @@ TRNSPARSE_API int trnsparse_bsr_richardson(int64_t m, int64_t n, int b, int64_t 
                              const int* col_idx, const float* blocks, const float* b_vec, double omega,
                              int K, float* x, float* work, double* rr_out, void* stream);
 
+/* Row-shard steps for the block-row-sharded fixed-step solvers and power
+ * iteration (the reference's chebyshev_bsr / richardson_bsr /
+ * power_iteration_bsr loops, iterative.py:193-340, split across ranks; the
+ * caller refreshes halo columns and reduces partial sums between steps).
+ * The BSR is the rank's shard: m own rows, n own + halo columns.
+ *   chebyshev_step: xnext = xk + a (b - A xk) [+ bcoef (xk - xprev)]
+ *                   (own rows; xk has its halo filled; richardson: momentum 0).
+ *   residual_sq:    *acc += ||b - A x||^2 over the own rows.
+ *   power_step:     w = A v (own rows); dots[0] += v.w, dots[1] += w.w.
+ *   vec_div_norm:   y = x / fp32(sqrt(*ss)). */
+TRNSPARSE_API int trnsparse_bsr_chebyshev_step(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                                  const int* col_idx, const float* blocks, const float* b_vec,
+                                  const float* xk, const float* xprev, float* xnext, double a, double bcoef,
+                                  int momentum, void* stream);
+TRNSPARSE_API int trnsparse_bsr_residual_sq(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                               const int* col_idx, const float* blocks, const float* b_vec, const float* x,
+                               double* acc, void* stream);
+TRNSPARSE_API int trnsparse_bsr_power_step(int64_t m, int64_t n, int b, int64_t n_blocks, const int* row_ptr,
+                              const int* col_idx, const float* blocks, const float* v, float* w, double* dots,
+                              void* stream);
+TRNSPARSE_API int trnsparse_vec_div_norm(int64_t n, const float* x, const double* ss, float* y, void* stream);
+
 /* acc = u . v accumulated in float64 (device scalar). */
 TRNSPARSE_API int trnsparse_dot(int64_t n, const float* u, const float* v, double* acc, void* stream);
 

@@ -108,3 +108,54 @@ def test_cgcg_peer_timeout_is_reported():
     # the context is still usable
     y = ts.bsr_spmm(A, bd.unsqueeze(1))
     assert torch.isfinite(y).all()
+
+
+def _worker_fixed(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        import trnsparse_b200 as ts
+        from trnsparse_b200 import distributed as D, workloads as w
+
+        A, b = w.block_pentadiagonal_spd(48)
+        sh = D.shard_bsr(A, rank, world)
+        bl = b[sh.r0 * 128 : sh.r1 * 128].cuda()
+        v0 = torch.randn(A.shape[0], generator=torch.Generator().manual_seed(7))
+        res = {}
+        for name, run_sh, run_1 in [
+            ("cheb", lambda: D.chebyshev_bsr_sharded(sh, bl, 4.0, 16.0, K=20),
+             lambda: ts.chebyshev_bsr(A, b.cuda(), 4.0, 16.0, K=20)),
+            ("rich", lambda: D.richardson_bsr_sharded(sh, bl, 0.09, K=15),
+             lambda: ts.richardson_bsr(A, b.cuda(), 0.09, K=15)),
+        ]:
+            x, K, rel = run_sh()
+            parts = [torch.zeros(D.shard_bsr(A, q, world).n_own, device="cuda") for q in range(world)]
+            dist.all_gather(parts, x.contiguous())
+            xr, Kr, relr = run_1()
+            res[name] = ((torch.linalg.norm(torch.cat(parts) - xr) / torch.linalg.norm(xr)).item(), K, Kr, rel, relr)
+        lam, v, it = D.power_iteration_bsr_sharded(sh, v0[sh.r0 * 128 : sh.r1 * 128].cuda(), max_iter=60, tol=1e-6)
+        parts = [torch.zeros(D.shard_bsr(A, q, world).n_own, device="cuda") for q in range(world)]
+        dist.all_gather(parts, v.contiguous())
+        lr, vr, itr = ts.power_iteration_bsr(A, v0.cuda(), max_iter=60, tol=1e-6)
+        res["power"] = ((torch.linalg.norm(torch.cat(parts) - vr) / torch.linalg.norm(vr)).item(), it, itr, lam, lr)
+        if rank == 0:
+            out.update(res)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_sharded_chebyshev_richardson_power(world):
+    """Block-row-sharded fixed-step solvers and power iteration against the single-GPU
+    ones (1e-5 relative on the solution / eigenvector, identical step counts)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    mp.start_processes(_worker_fixed, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
+    for name in ("cheb", "rich"):
+        err, K, Kr, rel, relr = out[name]
+        assert err <= 1e-5 and K == Kr and abs(rel - relr) <= 1e-4 * max(relr, 1e-12) + 1e-7, (name, out[name])
+    err, it, itr, lam, lr = out["power"]
+    assert err <= 1e-4 and abs(it - itr) <= 1 and abs(lam - lr) <= 1e-5 * abs(lr), out["power"]

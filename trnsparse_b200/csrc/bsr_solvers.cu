@@ -407,6 +407,42 @@ struct PowStart {
   __device__ void finish(double t0, double) const { atomicAdd(&w.slots[0].b, t0); }
 };
 
+// ---------------------------------------------------------------- row-shard steps
+// One step of the fixed-step solvers / power iteration on a block-row shard
+// (m own rows, n = own + halo columns); the caller refreshes the halo and
+// reduces the partial sums across ranks between steps.
+struct PowStepMv {
+  static constexpr int kDots = 2;
+  const float* vin;
+  float* wout;
+  double* dots;  // [0] += v.w, [1] += w.w over the own rows
+  __device__ bool begin(int) const { return true; }
+  __device__ float x(int64_t c) const { return vin[c]; }
+  __device__ float4 x4(int64_t c) const { return ld4(vin + c); }
+  __device__ void row(int64_t i, float y, double* d0, double* d1) const {
+    wout[i] = y;
+    *d0 += (double)vin[i] * (double)y;
+    *d1 += (double)y * (double)y;
+  }
+  __device__ void finish(double t0, double t1) const {
+    atomicAdd(&dots[0], t0);
+    atomicAdd(&dots[1], t1);
+  }
+};
+
+struct DivNorm {
+  const float* x;
+  const double* ss;
+  float* y;
+  mutable float nrm;
+  __device__ bool begin(int) const {
+    nrm = (float)sqrt(*ss);
+    return true;
+  }
+  __device__ void elem(int64_t i, double*, double*) const { y[i] = __fdiv_rn(x[i], nrm); }
+  __device__ void finish(double, double) const {}
+};
+
 // ---------------------------------------------------------------- helpers
 int check_desc(const BsrDesc& d, const char* what) {
   if (d.m < 0 || d.n < 0 || d.b <= 0 || d.n_blocks < 0)
@@ -450,6 +486,42 @@ extern "C" int trnsparse_bsr_spmv(BSR_DESC_ARGS, const float* x, double alpha, c
   if (y && beta == 0.0) y = nullptr;
   PlainOp op{x, y, out, (float)alpha, (float)beta};
   return launch_bsr_mv(d, op, all_aligned({x}), as_stream(stream), "bsr_spmv launch");
+}
+
+extern "C" int trnsparse_bsr_chebyshev_step(BSR_DESC_ARGS, const float* b_vec, const float* xk, const float* xprev,
+                                            float* xnext, double a, double bcoef, int momentum, void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_chebyshev_step");
+  if (rc) return rc;
+  TSB_REQUIRE(b_vec && xk && xnext && (!momentum || xprev), "bsr_chebyshev_step: null pointer");
+  if (m == 0) return TRNSPARSE_OK;
+  ChebMv op{b_vec, xk, xprev, xnext, (float)a, (float)bcoef, momentum != 0};
+  return launch_bsr_mv(d, op, all_aligned({xk}), as_stream(stream), "bsr_chebyshev_step");
+}
+
+extern "C" int trnsparse_bsr_residual_sq(BSR_DESC_ARGS, const float* b_vec, const float* x, double* acc,
+                                         void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_residual_sq");
+  if (rc) return rc;
+  TSB_REQUIRE(b_vec && x && acc, "bsr_residual_sq: null pointer");
+  if (m == 0) return TRNSPARSE_OK;
+  return launch_bsr_mv(d, ResidualMv{b_vec, x, acc}, all_aligned({x}), as_stream(stream), "bsr_residual_sq");
+}
+
+extern "C" int trnsparse_bsr_power_step(BSR_DESC_ARGS, const float* v, float* w, double* dots, void* stream) {
+  const BsrDesc d = BSR_DESC;
+  int rc = check_desc(d, "bsr_power_step");
+  if (rc) return rc;
+  TSB_REQUIRE(v && w && dots, "bsr_power_step: null pointer");
+  if (m == 0) return TRNSPARSE_OK;
+  return launch_bsr_mv(d, PowStepMv{v, w, dots}, all_aligned({v}), as_stream(stream), "bsr_power_step");
+}
+
+extern "C" int trnsparse_vec_div_norm(int64_t n, const float* x, const double* ss, float* y, void* stream) {
+  TSB_REQUIRE(n >= 0 && (n == 0 || (x && ss && y)), "vec_div_norm: bad argument");
+  if (n == 0) return TRNSPARSE_OK;
+  return launch_vec(n, DivNorm{x, ss, y, 0.f}, as_stream(stream), "vec_div_norm");
 }
 
 extern "C" size_t trnsparse_bsr_cg_workspace_size(int64_t n, int max_iter) {

@@ -480,14 +480,29 @@ csr_spmm_kernel(int64_t m, int64_t k, int64_t nnz, const I* __restrict__ rp, con
         T acc[VEC];
 #pragma unroll
         for (int q = 0; q < VEC; ++q) acc[q] = T(0);
-        for (int64_t j = a; j < b; ++j) {
-          T val; int64_t col;
-          if (st.fits) { val = vs[st.dv + j]; col = static_cast<int64_t>(cs[st.dc + j]); }
-          else { val = __ldg(v + st.s + j); col = static_cast<int64_t>(__ldg(ci + st.s + j)); }
-          const VT bv = __ldg(reinterpret_cast<const VT*>(B + col * ldb) + c);
-          const T* bp = reinterpret_cast<const T*>(&bv);
+        const VT* bc = reinterpret_cast<const VT*>(B) + c;
+        const int64_t ldv = ldb / VEC;
+        // unrolled so several independent B-row loads are in flight per group
+        if (st.fits) {
+          const T* vv = vs + st.dv;
+          const I* cc = cs + st.dc;
+#pragma unroll 4
+          for (int j = static_cast<int>(a); j < static_cast<int>(b); ++j) {
+            const VT bv = __ldg(bc + static_cast<int64_t>(cc[j]) * ldv);
+            const T val = vv[j];
+            const T* bp = reinterpret_cast<const T*>(&bv);
 #pragma unroll
-          for (int q = 0; q < VEC; ++q) acc[q] += val * bp[q];
+            for (int q = 0; q < VEC; ++q) acc[q] += val * bp[q];
+          }
+        } else {
+#pragma unroll 4
+          for (int64_t j = a; j < b; ++j) {
+            const VT bv = __ldg(bc + static_cast<int64_t>(__ldg(ci + st.s + j)) * ldv);
+            const T val = __ldg(v + st.s + j);
+            const T* bp = reinterpret_cast<const T*>(&bv);
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc[q] += val * bp[q];
+          }
         }
         VT o;
         T* op = reinterpret_cast<T*>(&o);
@@ -591,7 +606,8 @@ int launch_spmm(int64_t m, int64_t k, int64_t nnz, const void* rp, const void* c
   int G = 1;
   while (G < 32 && G < nchunk) G *= 2;
   // rows per CTA: enough row-groups to fill the CTA, and a slice that fits
-  const int rows = pick_rows(m, nnz, 2048);
+  static const int target = env_int("TRNSPARSE_SPMM_TILE", 4096);  // stored entries staged per CTA
+  const int rows = pick_rows(m, nnz, target);
   const double avg = m > 0 ? static_cast<double>(nnz) / m : 0.0;
   int cap = static_cast<int>(rows * avg * 1.25) + 256;
   if (cap > 8192) cap = 8192;

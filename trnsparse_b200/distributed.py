@@ -426,3 +426,100 @@ def cg_bsr_sharded(
     every rank). ``b_local`` is the rank's n_own-long slice of b; the Jacobi
     preconditioner (iterative.py:129-145) is applied when ``jacobi``."""
     return ShardedCG(shard, b_local, tol, max_iter, jacobi, group, check_every).run()
+
+
+# ---------------------------------------------------------------- fixed-step solvers, power iteration
+def _shard_setup(shard: BSRShard, vec: torch.Tensor):
+    from . import _lib
+    from .ops import _bsr_geometry
+
+    dev = vec.device
+    return _lib, _bsr_geometry(shard.local, dev), _lib.stream_handle(dev), dev
+
+
+def _global_sq(local_sq: torch.Tensor, group) -> float:
+    """Sum of a float64 device scalar over the ranks (rank order is NCCL's, so the
+    total may differ from a single-GPU sum in the last bit)."""
+    dist.all_reduce(local_sq, group=group)
+    return float(local_sq.item())
+
+
+def _fixed_step_sharded(shard: BSRShard, b_local: torch.Tensor, coeffs, K: int, x0_local, group):
+    lib, geo, s, dev = _shard_setup(shard, b_local)
+    n_own, n_ext = shard.n_own, shard.n_ext
+    b = b_local.to(dev, torch.float32).contiguous()
+    bb = torch.sum(b.double() * b.double()).reshape(1)
+    b_norm = float(torch.tensor(_global_sq(bb, group) ** 0.5, dtype=torch.float32))
+    # three extended buffers rotate: x_k (halo refreshed before each step), x_{k-1}, x_{k+1}
+    bufs = [torch.zeros(n_ext, dtype=torch.float32, device=dev) for _ in range(3)]
+    if x0_local is not None:
+        bufs[0][:n_own] = x0_local.to(dev, torch.float32)
+    with torch.cuda.device(dev):
+        for k in range(K):
+            xk, xp, xn = bufs[k % 3], bufs[(k + 2) % 3], bufs[(k + 1) % 3]
+            halo_exchange(shard, xk, group)
+            a, bc = coeffs(k)
+            lib.call("trnsparse_bsr_chebyshev_step", *geo, b.data_ptr(), xk.data_ptr(), xp.data_ptr(), xn.data_ptr(),
+                     a, 0.0 if bc is None else bc, 1 if k > 0 and bc is not None else 0, s)
+        x = bufs[K % 3]
+        halo_exchange(shard, x, group)
+        rr = torch.zeros(1, dtype=torch.float64, device=dev)
+        lib.call("trnsparse_bsr_residual_sq", *geo, b.data_ptr(), x.data_ptr(), rr.data_ptr(), s)
+    r_norm = float(torch.tensor(_global_sq(rr, group) ** 0.5, dtype=torch.float32))
+    return x[:n_own].clone(), K, r_norm / max(b_norm, 1e-15)
+
+
+def chebyshev_bsr_sharded(shard: BSRShard, b_local: torch.Tensor, lam_min: float, lam_max: float, K: int = 50,
+                          x0_local: torch.Tensor | None = None, group=None) -> tuple[torch.Tensor, int, float]:
+    """K-step Chebyshev semi-iteration (reference: iterative.py:193-253) on a
+    block-row shard: per step the halo rows of x are refreshed (NCCL
+    send/recv), then one fused SpMV + update launch runs on the own rows; the
+    final relative residual is reduced across the ranks. Returns this rank's
+    slice of x, K and rel (identical on every rank)."""
+    from .iterative import chebyshev_coeffs
+
+    alpha, beta = chebyshev_coeffs(lam_min, lam_max, K)
+    al, be = alpha.tolist(), beta.tolist()
+    return _fixed_step_sharded(shard, b_local, lambda k: (al[k], be[k] if k > 0 else 0.0), K, x0_local, group)
+
+
+def richardson_bsr_sharded(shard: BSRShard, b_local: torch.Tensor, omega: float, K: int = 100,
+                           x0_local: torch.Tensor | None = None, group=None) -> tuple[torch.Tensor, int, float]:
+    """K-step Richardson ``x += omega (b - A x)`` (reference: iterative.py:256-295) on a block-row shard."""
+    w = float(omega)
+    return _fixed_step_sharded(shard, b_local, lambda k: (w, None), K, x0_local, group)
+
+
+def power_iteration_bsr_sharded(shard: BSRShard, v0_local: torch.Tensor, max_iter: int = 100, tol: float = 1e-9,
+                                group=None) -> tuple[float, torch.Tensor, int]:
+    """Dominant eigenpair by power iteration (reference: iterative.py:298-340)
+    on a block-row shard. Per iteration: halo refresh of v, one SpMV launch
+    that also forms the partial v.Av and ||Av||^2, one all-reduce of the two
+    partials, then v = Av / ||Av|| on the device. The host reads the two
+    reduced scalars each iteration for the reference's stopping tests.
+    Returns (eigenvalue, this rank's slice of v, iterations)."""
+    lib, geo, s, dev = _shard_setup(shard, v0_local)
+    n_own, n_ext = shard.n_own, shard.n_ext
+    v = torch.zeros(n_ext, dtype=torch.float32, device=dev)
+    w = torch.zeros(n_own, dtype=torch.float32, device=dev)
+    v0 = v0_local.to(dev, torch.float32).contiguous()
+    ss = torch.sum(v0.double() * v0.double()).reshape(1)
+    dist.all_reduce(ss, group=group)
+    dots = torch.zeros(2, dtype=torch.float64, device=dev)
+    lam_prev, lam = 0.0, 0.0
+    with torch.cuda.device(dev):
+        lib.call("trnsparse_vec_div_norm", n_own, v0.data_ptr(), ss.data_ptr(), v.data_ptr(), s)
+        for k in range(max_iter):
+            halo_exchange(shard, v, group)
+            dots.zero_()
+            lib.call("trnsparse_bsr_power_step", *geo, v.data_ptr(), w.data_ptr(), dots.data_ptr(), s)
+            dist.all_reduce(dots, group=group)
+            lam, ww = dots.tolist()
+            norm = float(torch.tensor(ww ** 0.5, dtype=torch.float32))
+            if norm < 1e-30:
+                return 0.0, v[:n_own].clone(), k + 1
+            lib.call("trnsparse_vec_div_norm", n_own, w.data_ptr(), dots[1:].data_ptr(), v.data_ptr(), s)
+            if abs(lam - lam_prev) < tol:
+                return lam, v[:n_own].clone(), k + 1
+            lam_prev = lam
+    return lam, v[:n_own].clone(), max_iter
