@@ -251,6 +251,23 @@ TRNSPARSE_API int trnsparse_bsr_attention(int64_t heads, int64_t seq, int64_t he
                             const void* K, const void* V, void* O, int dtype, double scale,
                             void* stream);
 
+/* Block-sparse attention backward (reference: _block_sparse_attn_backward,
+ * trnsparse/ops.py:360-473; nki_bsr_attn_bwd, trnsparse/nki/dispatch.py:813):
+ * dQ, dK, dV of O = softmax(Q K^T scale) V over the stored blocks, by the
+ * Flash-delta identity dS = P (dO V^T - rowsum(dO o O)). Layout and dtypes as
+ * trnsparse_bsr_attention; head_dim <= 128. block_col_ptr / block_row_idx:
+ * the mask's transposed pattern (ceil(seq/b) + 1 column pointers; for each
+ * key block, the query blocks that store it). Workspace:
+ * trnsparse_bsr_attention_backward_workspace_size(heads, seq) bytes (row
+ * max, row sum, delta). Rows that get no gradient are zero. */
+TRNSPARSE_API size_t trnsparse_bsr_attention_backward_workspace_size(int64_t heads, int64_t seq);
+TRNSPARSE_API int trnsparse_bsr_attention_backward(int64_t heads, int64_t seq, int64_t head_dim, int block_size,
+                                      const int* block_row_ptr, const int* block_col_idx,
+                                      const int* block_col_ptr, const int* block_row_idx, const void* Q,
+                                      const void* K, const void* V, const void* O, const void* dO, void* dQ,
+                                      void* dK, void* dV, int dtype, double scale, void* ws, size_t ws_bytes,
+                                      void* stream);
+
 /* Tensor-core form of trnsparse_bsr_attention for bf16, block size 128,
  * head_dim 64 or 128, seq a multiple of 128: tcgen05 S = Q K^T and O += P V
  * with TMEM accumulators, in the reference's two-pass softmax form (row max

@@ -23,6 +23,7 @@ __all__ = [
     "screened_spmm",
     "screened_spmm_pair",
     "block_sparse_attention",
+    "block_sparse_attention_backward",
     "bsr_diagonal",
     "bsr_matvec",
     "cg_bsr",
@@ -199,6 +200,62 @@ def block_sparse_attention(Q, K, V, block_row_ptrs, block_col_indices, block_siz
 
 
 # --------------------------------------------------------------------------- solvers
+def block_sparse_attention_backward(Q, K, V, O, dO, block_row_ptrs, block_col_indices, block_size, scale=None):
+    """trnsparse/ops.py:360-473 (the recompute path: no saved row statistics).
+
+    D = rowsum(dO o O); row max and denominator recomputed in two passes over
+    the stored blocks (empty block rows: max 0), denominator clamped at
+    1e-12; then per stored block P = exp(s - max) / denom, dP = dO V^T,
+    dS = P (dP - D), dQ += dS K scale, dK += dS^T Q scale, dV += P^T dO.
+    Returns (dQ, dK, dV) in Q's dtype.
+    """
+    seq_len, head_dim = Q.shape
+    if scale is None:
+        scale = head_dim**-0.5
+    b = block_size
+    mt = seq_len // b
+    rp = [int(v) for v in block_row_ptrs.tolist()]
+    ci = [int(v) for v in block_col_indices.tolist()]
+    D = (dO * O).sum(dim=-1)
+    rmax = torch.full((seq_len,), float("-inf"), dtype=Q.dtype)
+    for m in range(mt):
+        sl = slice(m * b, (m + 1) * b)
+        if rp[m] == rp[m + 1]:
+            rmax[sl] = 0.0
+            continue
+        q = Q[sl]
+        rm = rmax[sl]
+        for idx in range(rp[m], rp[m + 1]):
+            c = ci[idx]
+            s = (q @ K[c * b : (c + 1) * b].T) * scale
+            rm = torch.maximum(rm, s.max(dim=1).values)
+        rmax[sl] = rm
+    rden = torch.zeros(seq_len, dtype=Q.dtype)
+    for m in range(mt):
+        sl = slice(m * b, (m + 1) * b)
+        q = Q[sl]
+        for idx in range(rp[m], rp[m + 1]):
+            c = ci[idx]
+            s = (q @ K[c * b : (c + 1) * b].T) * scale
+            rden[sl] += torch.exp(s - rmax[sl].unsqueeze(1)).sum(dim=1)
+    rden = rden.clamp(min=1e-12)
+    dQ, dK, dV = torch.zeros_like(Q), torch.zeros_like(K), torch.zeros_like(V)
+    for m in range(mt):
+        sl = slice(m * b, (m + 1) * b)
+        q, do, d = Q[sl], dO[sl], D[sl]
+        for idx in range(rp[m], rp[m + 1]):
+            c = ci[idx]
+            kb, vb = K[c * b : (c + 1) * b], V[c * b : (c + 1) * b]
+            s = (q @ kb.T) * scale
+            P = torch.exp(s - rmax[sl].unsqueeze(1)) / rden[sl].unsqueeze(1)
+            dP = do @ vb.T
+            dS = P * (dP - d.unsqueeze(1))
+            dQ[sl] += dS @ kb * scale
+            dK[c * b : (c + 1) * b] += dS.T @ q * scale
+            dV[c * b : (c + 1) * b] += P.T @ do
+    return dQ, dK, dV
+
+
 def bsr_diagonal(blocks, block_col_indices, block_row_ptrs, shape, block_size):
     """trnsparse/iterative.py:22-41."""
     m = shape[0]

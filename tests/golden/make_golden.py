@@ -162,6 +162,25 @@ m[:128, :128] = True
 m[256:, 128:] = True  # block-row 1 is empty -> zero output rows
 add_attn("attn_empty_row", 384, 64, 128, m, seed=15)
 
+# ---------------------------------------------------------------- attention backward (fp32)
+from trnsparse.ops import _block_sparse_attn_backward  # noqa: E402
+
+
+def add_attn_bwd(name, seq, hd, b, mask, seed):
+    torch.manual_seed(seed)
+    Q, K, V, dO = (torch.randn(seq, hd) for _ in range(4))
+    mb = trnsparse.BSRMatrix.from_dense(mask.float(), block_size=b)
+    O = trnsparse.block_sparse_attention_tiled(Q, K, V, mb)
+    dQ, dK, dV = _block_sparse_attn_backward(Q, K, V, O, dO, mb, hd**-0.5)
+    cases[name] = {"op": "attention_bwd", "Q": Q, "K": K, "V": V, "O": O, "dO": dO,
+                   "block_row_ptrs": mb.block_row_ptrs, "block_col_indices": mb.block_col_indices,
+                   "block_size": b, "dQ": dQ, "dK": dK, "dV": dV}
+
+
+add_attn_bwd("attn_bwd_local", 256, 32, 128, attn_demo._local_window_mask(256, 128, 1), seed=31)
+add_attn_bwd("attn_bwd_global", 384, 64, 128, attn_demo._global_token_mask(384, 128, 1, 1), seed=32)
+add_attn_bwd("attn_bwd_empty_row", 384, 32, 128, m, seed=33)
+
 # ---------------------------------------------------------------- solvers
 def spd(n, b, seed):
     torch.manual_seed(seed)

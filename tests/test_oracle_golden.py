@@ -137,3 +137,12 @@ def test_chebyshev_richardson_power():
     lam, v, it = oracle.power_iteration_bsr(_bsr(c), c["v0"], max_iter=c["max_iter"], tol=c["tol"])
     assert lam == c["lam"] and it == c["iters"]
     torch.testing.assert_close(v, c["v"], atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("name", golden_names("attention_bwd"))
+def test_attention_backward(name):
+    c = golden_cases()[name]
+    dQ, dK, dV = oracle.block_sparse_attention_backward(c["Q"], c["K"], c["V"], c["O"], c["dO"], c["block_row_ptrs"],
+                                                        c["block_col_indices"], c["block_size"])
+    for got, ref in ((dQ, c["dQ"]), (dK, c["dK"]), (dV, c["dV"])):
+        torch.testing.assert_close(got, ref, atol=0, rtol=0)

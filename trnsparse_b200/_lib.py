@@ -70,6 +70,9 @@ SIGNATURES.update({
                                    _i32, _p],
     "trnsparse_bsr_cg_fused_start": [_i64, _i64, _i32, _p, _p, _i32, _p, _sz, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_fused_phase": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
+    "trnsparse_bsr_attention_backward_workspace_size": [_i64, _i64],
+    "trnsparse_bsr_attention_backward": [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32,
+                                         _f64, _p, _sz, _p],
     "trnsparse_bsr_chebyshev_step": _BSR + [_p, _p, _p, _p, _f64, _f64, _i32, _p],
     "trnsparse_bsr_residual_sq": _BSR + [_p, _p, _p, _p],
     "trnsparse_bsr_power_step": _BSR + [_p, _p, _p, _p],
@@ -87,6 +90,7 @@ _RESTYPE = {
     "trnsparse_bsr_power_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_workspace_size": C.c_size_t,
     "trnsparse_bsr_cgcg_workspace_size": C.c_size_t,
+    "trnsparse_bsr_attention_backward_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_plan_capacity": C.c_int64,
     "trnsparse_screened_spmm_workspace_size": C.c_size_t,
     "trnsparse_peer_comm_bytes": C.c_size_t,

@@ -414,12 +414,53 @@ def _attn_dense_mask(mask_bsr, seq, dev):
     return m.to(dev)
 
 
+def _mask_indices(mask_bsr, dev):
+    """Block-row pointers / column indices of the mask and its transposed
+    pattern (column pointers / row indices), int32 on ``dev``; cached with the
+    mask's device layout when it has one."""
+    lay = mask_bsr.device_layout(dev) if hasattr(mask_bsr, "device_layout") else {}
+    hit = lay.get("attn_csc")
+    if hit is not None:
+        return hit
+    rp_h = mask_bsr.block_row_ptrs.to(torch.int64).cpu()
+    ci_h = mask_bsr.block_col_indices.to(torch.int64).cpu()
+    n_rows = rp_h.numel() - 1
+    n_cols = -(-mask_bsr.shape[1] // mask_bsr.block_size)
+    rows = torch.repeat_interleave(torch.arange(n_rows), rp_h[1:] - rp_h[:-1])
+    order = torch.argsort(ci_h * max(n_rows, 1) + rows, stable=True)
+    cp_h = torch.zeros(n_cols + 1, dtype=torch.int64)
+    cp_h[1:] = torch.cumsum(torch.bincount(ci_h, minlength=n_cols)[:n_cols], 0)
+    out = tuple(t.to(device=dev, dtype=torch.int32).contiguous() for t in (rp_h, ci_h, cp_h, rows[order]))
+    if lay is not None and hasattr(mask_bsr, "device_layout"):
+        lay["attn_csc"] = out
+    return out
+
+
+def _attn_backward(Q, K, V, O, dO, mask_bsr, scale):
+    """Device backward (reference: ops.py:360-473): stats, dQ (row-first) and
+    dK/dV (column-first over the transposed mask pattern) kernels."""
+    seq, hd = Q.shape[-2], Q.shape[-1]
+    dev = Q.device
+    rp, ci, cp, ri = _mask_indices(mask_bsr, dev)
+    b = mask_bsr.block_size
+    Qd, Kd, Vd, Od, dOd = (t.to(device=dev, dtype=Q.dtype).contiguous() for t in (Q, K, V, O, dO))
+    heads = Qd.numel() // (seq * hd) if seq * hd else 0
+    dQ, dK, dV = torch.empty_like(Qd), torch.empty_like(Kd), torch.empty_like(Vd)
+    ws_bytes = _lib.raw("trnsparse_bsr_attention_backward_workspace_size")(heads, seq)
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    code = _lib.F32 if Q.dtype == torch.float32 else _lib.BF16
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_bsr_attention_backward", heads, seq, hd, b, rp.data_ptr(), ci.data_ptr(), cp.data_ptr(),
+                  ri.data_ptr(), Qd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), Od.data_ptr(), dOd.data_ptr(),
+                  dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), code, float(scale), ws.data_ptr(), ws_bytes,
+                  _lib.stream_handle(dev))
+    return dQ, dK, dV
+
+
 class _AttnFunction(torch.autograd.Function):
-    """Autograd wrapper (reference: ops.py:476-546). Forward runs the CUDA
-    kernel; backward applies the reference's Flash-delta formulas
-    (ops.py:360-473) with dense masked torch ops on the device, which costs
-    O(seq^2) memory and is meant for training-sized problems, not the
-    long-sequence benchmark."""
+    """Autograd wrapper (reference: ops.py:476-546). Forward and backward
+    both run CUDA kernels; the backward follows the reference's Flash-delta
+    formulas (ops.py:360-473) over the stored blocks only."""
 
     @staticmethod
     def forward(ctx, Q, K, V, mask_bsr, scale):
@@ -431,22 +472,8 @@ class _AttnFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dO):
         Q, K, V, O = ctx.saved_tensors
-        seq = Q.shape[-2]
-        m = _attn_dense_mask(ctx.mask_bsr, seq, Q.device)
-        Qf, Kf, Vf, dOf, Of = (t.float() for t in (Q, K, V, dO.to(Q.device), O))
-        S = (Qf @ Kf.transpose(-1, -2)) * ctx.scale
-        S = S.masked_fill(~m, float("-inf"))
-        mx = S.amax(dim=-1, keepdim=True)
-        mx = torch.where(torch.isfinite(mx), mx, torch.zeros_like(mx))
-        P = torch.exp(S - mx)
-        P = P / P.sum(dim=-1, keepdim=True).clamp(min=1e-12)
-        D = (dOf * Of).sum(dim=-1, keepdim=True)
-        dP = dOf @ Vf.transpose(-1, -2)
-        dS = P * (dP - D)
-        dQ = (dS @ Kf) * ctx.scale
-        dK = (dS.transpose(-1, -2) @ Qf) * ctx.scale
-        dV = P.transpose(-1, -2) @ dOf
-        return dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype), None, None
+        dQ, dK, dV = _attn_backward(Q, K, V, O, dO, ctx.mask_bsr, ctx.scale)
+        return dQ.view_as(Q), dK.view_as(K), dV.view_as(V), None, None
 
 
 def block_sparse_attention_tiled(
