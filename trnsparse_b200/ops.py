@@ -11,6 +11,7 @@ compute path and no backend switch.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -59,11 +60,21 @@ def spmv(
 
     ``beta * y`` is added only when ``y is not None and beta != 0.0``. A 2-D
     ``x`` is treated as a dense right-hand side (as ``sparse @ x`` would).
+    Differentiable in ``A.values``, ``x`` and ``y`` (as the reference's torch
+    path is); the backward runs the transposed product on the device.
     """
     m, n = A.shape
     assert x.shape[0] == n, f"Dimension mismatch: A is {A.shape}, x is {x.shape}"
     if x.dim() == 2:
         return spmm(A, x, alpha=alpha, C=y, beta=beta)
+    if _needs_grad(A.values, x, y):
+        use_y = y is not None and beta != 0.0
+        return _CsrProductFn.apply(A.values, x, y if use_y else None, A, float(alpha), float(beta))
+    return _spmv_impl(A, x, alpha, y, beta)
+
+
+def _spmv_impl(A: CSRMatrix, x: torch.Tensor, alpha: float, y, beta: float) -> torch.Tensor:
+    m, n = A.shape
     dev = _dev_of(x)
     if x.dtype != A.dtype:
         raise RuntimeError(f"spmv: dtype mismatch, A is {A.dtype} and x is {x.dtype}")
@@ -90,11 +101,20 @@ def spmm(
     C: torch.Tensor | None = None,
     beta: float = 0.0,
 ) -> torch.Tensor:
-    """``alpha * A @ B (+ beta * C)`` (reference: trnsparse/ops.py:51-78)."""
+    """``alpha * A @ B (+ beta * C)`` (reference: trnsparse/ops.py:51-78).
+    Differentiable in ``A.values``, ``B`` and ``C``."""
     m, n = A.shape
     assert B.shape[0] == n, f"Dimension mismatch: A is {A.shape}, B is {B.shape}"
     if B.dim() == 1:
         return spmv(A, B, alpha=alpha, y=C, beta=beta)
+    if _needs_grad(A.values, B, C):
+        use_c = C is not None and beta != 0.0
+        return _CsrProductFn.apply(A.values, B, C if use_c else None, A, float(alpha), float(beta))
+    return _spmm_impl(A, B, alpha, C, beta)
+
+
+def _spmm_impl(A: CSRMatrix, B: torch.Tensor, alpha: float, C, beta: float) -> torch.Tensor:
+    m, n = A.shape
     dev = _dev_of(B)
     if B.dtype != A.dtype:
         raise RuntimeError(f"spmm: dtype mismatch, A is {A.dtype} and B is {B.dtype}")
@@ -247,8 +267,17 @@ def bsr_spmm(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
     on the GPU: one right-hand-side column runs the HBM-bound BSR SpMV
     kernel; block size 128 runs the tcgen05 tensor-core kernel (3xTF32 for
     float32, bf16 operands with fp32 accumulation for bfloat16); other block
-    sizes run the CUDA-core kernel (float32 FMA).
+    sizes run the CUDA-core kernel (float32 FMA). Differentiable in
+    ``A.blocks`` and ``B``: dB = A^T dC runs the same kernels on the cached
+    transposed matrix, dblocks[k] = dC[rows(k)] B[cols(k)]^T is one batched
+    GEMM over the stored blocks.
     """
+    if _needs_grad(A.blocks, B):
+        return _BsrSpmmFn.apply(A.blocks, B, A)
+    return _bsr_spmm_impl(A, B)
+
+
+def _bsr_spmm_impl(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
     m, n = A.shape
     if B.shape[0] != n:
         raise AssertionError(f"Dimension mismatch: A is {A.shape}, B is {tuple(B.shape)}")
@@ -288,6 +317,141 @@ def bsr_spmm(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
     return _back(out.to(A.dtype), B)
 
 
+# ---------------------------------------------------------------- autograd of the products
+def _needs_grad(*ts) -> bool:
+    return torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in ts)
+
+
+def _csr_transpose(A: CSRMatrix) -> tuple[CSRMatrix, torch.Tensor]:
+    """A^T as a CSRMatrix and, for each of its entries, the index of the entry of A
+    it came from (cached per A's fingerprint)."""
+    from .formats import _fingerprint
+
+    key = ("transpose", _fingerprint(A.values, A.col_indices, A.row_ptrs))
+    hit = A._dev.get(key)
+    if hit is not None:
+        return hit
+    m, n = A.shape
+    rp = A.row_ptrs.to(torch.long).cpu()
+    ci = A.col_indices.to(torch.long).cpu()
+    rows = torch.repeat_interleave(torch.arange(m), rp[1:] - rp[:-1])
+    order = torch.argsort(ci * max(m, 1) + rows, stable=True)
+    rpt = torch.zeros(n + 1, dtype=torch.long)
+    rpt[1:] = torch.cumsum(torch.bincount(ci, minlength=n)[:n], 0)
+    idx_t = A.row_ptrs.dtype if A.row_ptrs.dtype == A.col_indices.dtype else torch.long
+    AT = CSRMatrix(values=A.values.detach()[order.to(A.values.device)], col_indices=rows[order].to(idx_t),
+                   row_ptrs=rpt.to(idx_t), shape=(n, m))
+    A._dev[key] = (AT, order)
+    return AT, order
+
+
+def _csr_values_grad(A: CSRMatrix, dC: torch.Tensor, B: torch.Tensor, alpha: float) -> torch.Tensor:
+    """d values[j] = alpha * <dC[row_j], B[col_j]> (the product's adjoint projected on A's pattern)."""
+    dev = dC.device
+    rp = A.row_ptrs.to(device=dev, dtype=torch.long)
+    rows = torch.repeat_interleave(torch.arange(A.shape[0], device=dev), rp[1:] - rp[:-1])
+    cols = A.col_indices.to(device=dev, dtype=torch.long)
+    dC2 = dC.reshape(dC.shape[0], -1)
+    B2 = B.to(dev).reshape(B.shape[0], -1)
+    out = torch.empty(A.nnz, dtype=dC.dtype, device=dev)
+    step = max(1, (1 << 26) // max(dC2.shape[1], 1))
+    for s0 in range(0, A.nnz, step):
+        sl = slice(s0, s0 + step)
+        out[sl] = (dC2[rows[sl]] * B2[cols[sl]]).sum(dim=1)
+    return (alpha * out).to(A.values.device)
+
+
+class _CsrProductFn(torch.autograd.Function):
+    """alpha * A @ X (+ beta * Y) with X a vector or matrix: the adjoints are
+    dX = alpha * A^T dOut (the same device kernels on the cached transpose),
+    dY = beta * dOut, dvalues = alpha * <dOut[row], X[col]>."""
+
+    @staticmethod
+    def forward(ctx, values, X, Y, A, alpha, beta):
+        ctx.A, ctx.alpha, ctx.beta = A, alpha, beta
+        ctx.save_for_backward(X)
+        if X.dim() == 1:
+            return _spmv_impl(A, X, alpha, Y, beta)
+        return _spmm_impl(A, X, alpha, Y, beta)
+
+    @staticmethod
+    def backward(ctx, dout):
+        A, alpha, beta = ctx.A, ctx.alpha, ctx.beta
+        (X,) = ctx.saved_tensors
+        dvals = dX = dY = None
+        if ctx.needs_input_grad[1]:
+            AT, _ = _csr_transpose(A)
+            g = dout.to(X.device).contiguous()
+            dX = _spmv_impl(AT, g, alpha, None, 0.0) if X.dim() == 1 else _spmm_impl(AT, g, alpha, None, 0.0)
+        if ctx.needs_input_grad[2]:
+            dY = beta * dout
+        if ctx.needs_input_grad[0]:
+            dvals = _csr_values_grad(A, dout, X, alpha)
+        return dvals, dX, dY, None, None, None
+
+
+def _bsr_transpose(A: BSRMatrix) -> BSRMatrix:
+    """A^T as a BSRMatrix: transposed blocks in the transposed pattern's order (cached)."""
+    from .formats import _fingerprint
+
+    key = ("transpose", _fingerprint(A.blocks, A.block_col_indices, A.block_row_ptrs))
+    hit = A._dev.get(key)
+    if hit is not None:
+        return hit
+    b = A.block_size
+    rp = A.block_row_ptrs.to(torch.long).cpu()
+    ci = A.block_col_indices.to(torch.long).cpu()
+    R = rp.numel() - 1
+    Cn = -(-A.shape[1] // b)
+    rows = torch.repeat_interleave(torch.arange(R), rp[1:] - rp[:-1])
+    order = torch.argsort(ci * max(R, 1) + rows, stable=True)
+    rpt = torch.zeros(Cn + 1, dtype=torch.long)
+    rpt[1:] = torch.cumsum(torch.bincount(ci, minlength=Cn)[:Cn], 0)
+    blocks_t = A.blocks.detach()[order.to(A.blocks.device)].transpose(1, 2).contiguous()
+    AT = BSRMatrix(blocks=blocks_t, block_col_indices=rows[order], block_row_ptrs=rpt, shape=(A.shape[1], A.shape[0]),
+                   block_size=b)
+    A._dev[key] = AT
+    return AT
+
+
+def _bsr_blocks_grad(A: BSRMatrix, dC: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """dblocks[k] = dC[rows of block-row i] @ B[rows of block-column j]^T for
+    stored block k = (i, j): one batched GEMM over the gathered row blocks."""
+    b = A.block_size
+    dev = dC.device
+    R = A.block_row_ptrs.numel() - 1
+    Cn = -(-A.shape[1] // b)
+    k = dC.shape[1]
+    dCp = torch.zeros(R * b, k, dtype=torch.float32, device=dev)
+    dCp[: dC.shape[0]] = dC.float()
+    Bp = torch.zeros(Cn * b, k, dtype=torch.float32, device=dev)
+    Bp[: B.shape[0]] = B.to(dev).float()
+    rp = A.block_row_ptrs.to(device=dev, dtype=torch.long)
+    rows = torch.repeat_interleave(torch.arange(R, device=dev), rp[1:] - rp[:-1])
+    cols = A.block_col_indices.to(device=dev, dtype=torch.long)
+    g = torch.bmm(dCp.view(R, b, k)[rows], Bp.view(Cn, b, k)[cols].transpose(1, 2))
+    return g.to(dtype=A.blocks.dtype, device=A.blocks.device)
+
+
+class _BsrSpmmFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, blocks, B, A):
+        ctx.A = A
+        ctx.save_for_backward(B)
+        return _bsr_spmm_impl(A, B)
+
+    @staticmethod
+    def backward(ctx, dC):
+        A = ctx.A
+        (B,) = ctx.saved_tensors
+        dblocks = dB = None
+        if ctx.needs_input_grad[1]:
+            dB = _bsr_spmm_impl(_bsr_transpose(A), dC.to(device=B.device).contiguous()).to(B.dtype)
+        if ctx.needs_input_grad[0]:
+            dblocks = _bsr_blocks_grad(A, dC, B)
+        return dblocks, dB, None
+
+
 def bsr_spmm_cuda_core(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
     """``A @ B`` on the CUDA-core kernel (fp32 FMA): a second, independent
     device implementation used to cross-check the tensor-core path."""
@@ -322,7 +486,44 @@ def screened_spmm(
     ``Q = schwarz_bounds(G)``; ``mask = screen_quartets(Q, threshold)``,
     i.e. ``Q > sqrt(threshold)`` (trnsparse/screening.py:29-40).
     Comparisons are in float32, like the reference's tensor comparisons.
+    Differentiable in ``A`` and ``B`` (the mask is discrete, as in the
+    reference's _ScreenedSpMMFunction, nki/dispatch.py:447-484): dB runs the
+    same kernel on A^T with the transposed mask; dA = (dC B^T) o mask.
     """
+    if _needs_grad(A, B):
+        return _ScreenedFn.apply(A, B, diag_integrals, float(threshold))
+    return _screened_impl(A, diag_integrals, B, threshold)
+
+
+class _ScreenedFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, A, B, diag_integrals, threshold):
+        ctx.threshold = threshold
+        ctx.save_for_backward(A, B, diag_integrals)
+        return _screened_impl(A, diag_integrals, B, threshold)
+
+    @staticmethod
+    def backward(ctx, dC):
+        A, B, Q = ctx.saved_tensors
+        thr = ctx.threshold
+        dA = dB = None
+        if ctx.needs_input_grad[1]:
+            Qt = Q if Q.dim() == 1 else Q.t().contiguous()  # the 1-D mask is symmetric
+            dB = _screened_impl(A.detach().t().contiguous(), Qt, dC.contiguous(), thr).to(B.device)
+        if ctx.needs_input_grad[0]:
+            dev = dC.device
+            Qd = Q.to(device=dev, dtype=torch.float32)
+            t = float(torch.tensor(math.sqrt(thr), dtype=torch.float32))  # fp32(sqrt(threshold)), as the kernel
+            if Qd.dim() == 1:
+                q = torch.sqrt(torch.abs(Qd))
+                mask = q.unsqueeze(1) * q.unsqueeze(0) > t
+            else:
+                mask = Qd > t
+            dA = ((dC.float() @ B.to(dev).float().t()) * mask).to(A.device)
+        return dA, dB, None, None
+
+
+def _screened_impl(A: torch.Tensor, diag_integrals: torch.Tensor, B: torch.Tensor, threshold: float) -> torch.Tensor:
     M, K = A.shape
     if diag_integrals.dim() == 1:
         assert diag_integrals.shape[0] == M == K, (
