@@ -19,11 +19,21 @@ pytestmark = pytest.mark.gpu
 
 
 def _free_port() -> int:
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+    """A port that binds now, drawn at random from a high range (an ephemeral port the
+    OS just handed to the previous test's store can still be in TIME_WAIT)."""
+    import random
+
+    for _ in range(100):
+        p = random.randint(20000, 60000)
+        s = socket.socket()
+        try:
+            s.bind(("127.0.0.1", p))
+            return p
+        except OSError:
+            continue
+        finally:
+            s.close()
+    raise RuntimeError("no free port")
 
 
 def _worker(rank, world, port, cases, out, transport="nccl"):
