@@ -442,8 +442,12 @@ csr_spmv_warp_kernel(int64_t m, int64_t nnz, const I* __restrict__ rp, const I* 
 
 // SpMM: a group of G lanes owns one row; each lane owns VEC-wide column
 // chunks c = lane_in_group + G*t of the k output columns.
+// Eight CTAs per SM (32 registers) for 32-bit indices and values: the kernel
+// is memory-latency bound and occupancy is what keeps enough B-row loads in
+// flight (config 2b: 0.39 ms at four CTAs per SM, 0.30 ms at eight); the wider
+// instantiations would spill at 32 registers and keep four.
 template <typename I, typename T, int VEC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, (sizeof(I) == 4 && sizeof(T) == 4 && VEC > 1) ? 8 : 4)
 csr_spmm_kernel(int64_t m, int64_t k, int64_t nnz, const I* __restrict__ rp, const I* __restrict__ ci,
                 const T* __restrict__ v, const T* __restrict__ B, int64_t ldb, T alpha,
                 const T* __restrict__ C, int64_t ldc, T beta, T* __restrict__ out, int64_t ldo,
@@ -606,7 +610,7 @@ int launch_spmm(int64_t m, int64_t k, int64_t nnz, const void* rp, const void* c
   int G = 1;
   while (G < 32 && G < nchunk) G *= 2;
   // rows per CTA: enough row-groups to fill the CTA, and a slice that fits
-  static const int target = env_int("TRNSPARSE_SPMM_TILE", 4096);  // stored entries staged per CTA
+  static const int target = env_int("TRNSPARSE_SPMM_TILE", 2048);  // stored entries staged per CTA
   const int rows = pick_rows(m, nnz, target);
   const double avg = m > 0 ? static_cast<double>(nnz) / m : 0.0;
   int cap = static_cast<int>(rows * avg * 1.25) + 256;
