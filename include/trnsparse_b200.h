@@ -257,16 +257,19 @@ TRNSPARSE_API int trnsparse_bsr_attention(int64_t heads, int64_t seq, int64_t he
  * Flash-delta identity dS = P (dO V^T - rowsum(dO o O)). Layout and dtypes as
  * trnsparse_bsr_attention; head_dim <= 128. block_col_ptr / block_row_idx:
  * the mask's transposed pattern (ceil(seq/b) + 1 column pointers; for each
- * key block, the query blocks that store it). Workspace:
- * trnsparse_bsr_attention_backward_workspace_size(heads, seq) bytes (row
- * max, row sum, delta). Rows that get no gradient are zero. */
-TRNSPARSE_API size_t trnsparse_bsr_attention_backward_workspace_size(int64_t heads, int64_t seq);
+ * key block, the query blocks that store it); max_col_blocks: the largest
+ * number of query blocks storing one key block (more than 8 splits it over
+ * CTAs). Workspace: trnsparse_bsr_attention_backward_workspace_size(...)
+ * bytes (row max, row sum, delta; fp32 dK/dV accumulators for bf16 when a
+ * key block is split). Rows that get no gradient are zero. */
+TRNSPARSE_API size_t trnsparse_bsr_attention_backward_workspace_size(int64_t heads, int64_t seq, int64_t head_dim,
+                                                         int dtype, int max_col_blocks);
 TRNSPARSE_API int trnsparse_bsr_attention_backward(int64_t heads, int64_t seq, int64_t head_dim, int block_size,
                                       const int* block_row_ptr, const int* block_col_idx,
-                                      const int* block_col_ptr, const int* block_row_idx, const void* Q,
-                                      const void* K, const void* V, const void* O, const void* dO, void* dQ,
-                                      void* dK, void* dV, int dtype, double scale, void* ws, size_t ws_bytes,
-                                      void* stream);
+                                      const int* block_col_ptr, const int* block_row_idx, int max_col_blocks,
+                                      const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                                      void* dQ, void* dK, void* dV, int dtype, double scale, void* ws,
+                                      size_t ws_bytes, void* stream);
 
 /* Tensor-core form of trnsparse_bsr_attention for bf16, block size 128,
  * head_dim 64 or 128, seq a multiple of 128: tcgen05 S = Q K^T and O += P V

@@ -185,3 +185,28 @@ def test_attention_backward_bf16_heads_and_ragged():
         torch.testing.assert_close(got.cpu(), ref, atol=1e-4, rtol=1e-4)
     assert torch.count_nonzero(Qd.grad[192:]) == 0
     assert ts._lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_attention_backward_split_global_columns(dtype):
+    """A key block stored by more than 8 query blocks (a global-token column
+    of a 21-block mask) is split over several dK/dV CTAs that add into fp32
+    accumulators; checked against the fp32 oracle (1e-4 for fp32, 2e-2
+    relative Frobenius for bf16)."""
+    seq, hd, b = 21 * 64, 64, 64
+    mask = w.sliding_window_mask(seq=seq, b=b, window=2, n_global=1)
+    g = torch.Generator().manual_seed(77)
+    Q, K, V, dO = (torch.randn(seq, hd, generator=g).to(dtype) for _ in range(4))
+    Qd, Kd, Vd = (t.cuda().requires_grad_(True) for t in (Q, K, V))
+    ts.block_sparse_attention_tiled(Qd, Kd, Vd, mask).backward(dO.cuda())
+    args = [t.float() for t in (Q, K, V)]
+    O = oracle.block_sparse_attention(*args, mask.block_row_ptrs, mask.block_col_indices, b)
+    refs = oracle.block_sparse_attention_backward(*args, O, dO.float(), mask.block_row_ptrs,
+                                                  mask.block_col_indices, b)
+    for got, ref in zip((Qd.grad, Kd.grad, Vd.grad), refs):
+        assert got.dtype == dtype
+        if dtype == torch.float32:
+            torch.testing.assert_close(got.cpu(), ref, atol=1e-4, rtol=1e-4)
+        else:
+            assert rel_fro(got.float().cpu(), ref) <= 2e-2
+    assert ts._lib.device_error() == 0

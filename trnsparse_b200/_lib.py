@@ -70,9 +70,9 @@ SIGNATURES.update({
                                    _i32, _p],
     "trnsparse_bsr_cg_fused_start": [_i64, _i64, _i32, _p, _p, _i32, _p, _sz, _p, _i32, _i32, _sz, _p, _i32, _p],
     "trnsparse_bsr_cg_fused_phase": _BSR + [_p, _p, _f64, _i32, _i32, _i32, _p, _p, _i32, _i32, _sz, _p, _i32, _p],
-    "trnsparse_bsr_attention_backward_workspace_size": [_i64, _i64],
-    "trnsparse_bsr_attention_backward": [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32,
-                                         _f64, _p, _sz, _p],
+    "trnsparse_bsr_attention_backward_workspace_size": [_i64, _i64, _i64, _i32, _i32],
+    "trnsparse_bsr_attention_backward": [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _p, _p,
+                                         _i32, _f64, _p, _sz, _p],
     "trnsparse_bsr_chebyshev_step": _BSR + [_p, _p, _p, _p, _f64, _f64, _i32, _p],
     "trnsparse_bsr_residual_sq": _BSR + [_p, _p, _p, _p],
     "trnsparse_bsr_power_step": _BSR + [_p, _p, _p, _p],

@@ -632,6 +632,7 @@ def _mask_indices(mask_bsr, dev):
     cp_h = torch.zeros(n_cols + 1, dtype=torch.int64)
     cp_h[1:] = torch.cumsum(torch.bincount(ci_h, minlength=n_cols)[:n_cols], 0)
     out = tuple(t.to(device=dev, dtype=torch.int32).contiguous() for t in (rp_h, ci_h, cp_h, rows[order]))
+    out = out + (int((cp_h[1:] - cp_h[:-1]).max().item()) if n_cols > 0 else 0,)
     if lay is not None and hasattr(mask_bsr, "device_layout"):
         lay["attn_csc"] = out
     return out
@@ -642,17 +643,17 @@ def _attn_backward(Q, K, V, O, dO, mask_bsr, scale):
     dK/dV (column-first over the transposed mask pattern) kernels."""
     seq, hd = Q.shape[-2], Q.shape[-1]
     dev = Q.device
-    rp, ci, cp, ri = _mask_indices(mask_bsr, dev)
+    rp, ci, cp, ri, max_col = _mask_indices(mask_bsr, dev)
     b = mask_bsr.block_size
     Qd, Kd, Vd, Od, dOd = (t.to(device=dev, dtype=Q.dtype).contiguous() for t in (Q, K, V, O, dO))
     heads = Qd.numel() // (seq * hd) if seq * hd else 0
     dQ, dK, dV = torch.empty_like(Qd), torch.empty_like(Kd), torch.empty_like(Vd)
-    ws_bytes = _lib.raw("trnsparse_bsr_attention_backward_workspace_size")(heads, seq)
-    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
     code = _lib.F32 if Q.dtype == torch.float32 else _lib.BF16
+    ws_bytes = _lib.raw("trnsparse_bsr_attention_backward_workspace_size")(heads, seq, hd, code, max_col)
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         _lib.call("trnsparse_bsr_attention_backward", heads, seq, hd, b, rp.data_ptr(), ci.data_ptr(), cp.data_ptr(),
-                  ri.data_ptr(), Qd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), Od.data_ptr(), dOd.data_ptr(),
+                  ri.data_ptr(), max_col, Qd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), Od.data_ptr(), dOd.data_ptr(),
                   dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), code, float(scale), ws.data_ptr(), ws_bytes,
                   _lib.stream_handle(dev))
     return dQ, dK, dV
