@@ -424,16 +424,19 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
         "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "blocks_per_head": mask.n_blocks,
         "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 3), "peak": "bf16 measured",
         "note": "FLOPs counted once per block (QK^T + PV); the kernel's two-pass softmax recomputes QK^T"}
-    # config 4 backward (the survey's first "next" row): dQ, dK, dV on the CUDA cores
-    from trnsparse_b200.ops import _attn_backward
+    # config 4 backward (the survey's first "next" row): dQ, dK, dV on the tensor cores, with the
+    # forward's saved log-sum-exp (as autograd runs it)
+    from trnsparse_b200.ops import _attn_backward, _attn_forward
 
-    Oa = ts.block_sparse_attention_tiled(Qa, Ka, Va, mask)
+    Oa, lse = _attn_forward(Qa, Ka, Va, mask, 128 ** -0.5, want_lse=True)
     dOa = torch.randn(Oa.shape, generator=torch.Generator().manual_seed(5)).to(Oa.dtype).cuda()
-    ms = time_call(lambda: _attn_backward(Qa, Ka, Va, Oa, dOa, mask, 128 ** -0.5), 3, None)
+    ms = time_call(lambda: _attn_backward(Qa, Ka, Va, Oa, dOa, mask, 128 ** -0.5, lse=lse), 3, None)
     flb = 10 * 128 ** 3 * mask.n_blocks * 16
     ex["config4_attention_backward_bf16"] = {
         "TFLOP/s": round(flb / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 3),
-        "note": "CUDA-core kernels (fp32 FMA); FLOPs = S, dP, dQ, dK, dV per block (10*128^3)"}
+        "frac_of_peak": round(flb / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 3), "peak": "bf16 measured",
+        "note": "tcgen05 kernels (dQ row-first, dK/dV column-first); FLOPs = S, dP, dQ, dK, dV per block "
+                "(10*128^3), S and dP are computed in both passes"}
     del Qa, Ka, Va, Oa, dOa
     # config 5: Jacobi-PCG, 200 iterations, tol 0
     A5, b5 = w.block_pentadiagonal_spd()

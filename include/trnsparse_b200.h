@@ -278,6 +278,35 @@ TRNSPARSE_API int trnsparse_bsr_attention_backward(int64_t heads, int64_t seq, i
 TRNSPARSE_API int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t head_dim, const int* block_row_ptr,
                                const int* block_col_idx, const void* Q, const void* K, const void* V,
                                void* O, double scale, void* stream);
+/* As trnsparse_bsr_attention_tc; lse (nullable, fp32 [heads * seq]) receives
+ * each row's log-sum-exp in base-2 units of the scaled scores,
+ * log2(sum_j exp2(s_j * scale * log2(e))), which the tensor-core backward takes. */
+TRNSPARSE_API int trnsparse_bsr_attention_tc_lse(int64_t heads, int64_t seq, int64_t head_dim,
+                                   const int* block_row_ptr, const int* block_col_idx, const void* Q,
+                                   const void* K, const void* V, void* O, float* lse, double scale, void* stream);
+
+/* Tensor-core backward (bf16, block 128, head_dim 64/128, seq % 128 == 0) of
+ * the reference's _block_sparse_attn_backward (trnsparse/ops.py:360-473).
+ * The plan (host, int32) lists row units (query block, range of
+ * block_col_idx), column units (key block, range of block_row_idx of the
+ * transposed pattern) and aux entries (blocks with no stored partner, and
+ * blocks split over several units, whose partial sums go through fp32
+ * workspace slots); plan == NULL only fills counts = {row units, column
+ * units, aux entries, slots}. split bounds the partner blocks per unit. */
+TRNSPARSE_API int trnsparse_bsr_attention_backward_tc_plan(int64_t n_block_rows, int64_t n_block_cols,
+                                             const int* block_row_ptr, const int* block_col_ptr, int split,
+                                             int* plan, int64_t plan_capacity, int64_t* counts);
+TRNSPARSE_API size_t trnsparse_bsr_attention_backward_tc_workspace_size(int64_t heads, int64_t seq, int64_t head_dim,
+                                                          int64_t n_slots);
+/* plan: the device copy of the plan above (16-byte aligned). lse: the
+ * forward's trnsparse_bsr_attention_tc_lse output, or NULL (then the forward
+ * is rerun for it, into dQ as scratch). */
+TRNSPARSE_API int trnsparse_bsr_attention_backward_tc(int64_t heads, int64_t seq, int64_t head_dim,
+                                        const int* block_row_ptr, const int* block_col_idx,
+                                        const int* block_row_idx, const int* plan, int n_row_units,
+                                        int n_col_units, int n_aux, int n_slots, const void* Q, const void* K,
+                                        const void* V, const void* O, const void* dO, const float* lse, void* dQ,
+                                        void* dK, void* dV, double scale, void* ws, size_t ws_bytes, void* stream);
 
 /* ---- block-row-sharded CG (one process per GPU) --------------------------
  * The multi-GPU form of cg_bsr (trnsparse/iterative.py:53-126; the

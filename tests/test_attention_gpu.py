@@ -210,3 +210,69 @@ def test_attention_backward_split_global_columns(dtype):
         else:
             assert rel_fro(got.float().cpu(), ref) <= 2e-2
     assert ts._lib.device_error() == 0
+
+
+def _tc_backward_case(hd, heads, seq, rp, ci, seed):
+    g = torch.Generator().manual_seed(seed)
+    Q, K, V, dO = (torch.randn(1, heads, seq, hd, generator=g).to(torch.bfloat16) for _ in range(4))
+    m = _Mask(rp, ci, 128, seq)
+    return m, Q, K, V, dO
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("split", [16, 3])
+def test_attention_backward_tensor_core_vs_oracle(hd, split, monkeypatch):
+    """tcgen05 backward (bf16, block 128) against the fp32 oracle on the same
+    bf16 inputs, 2e-2 relative Frobenius: global-token columns stored by more
+    query blocks than `split` (partial sums through fp32 slots), an empty
+    block-row (zero dQ) and a key block no query block stores (zero dK, dV)."""
+    from trnsparse_b200 import ops
+
+    monkeypatch.setattr(ops, "_ATTN_BWD_SPLIT", split)
+    seq, heads = 128 * 20, 2
+    mt = seq // 128
+    keep = torch.zeros(mt, mt, dtype=torch.bool)
+    for i in range(mt):
+        for j in range(mt):
+            keep[i, j] = j <= i and (i - j < 3 or j < 2)
+    keep[5, :] = False      # empty block-row
+    keep[:, 7] = False      # key block stored by no query block
+    rows, cols = keep.nonzero(as_tuple=True)
+    rp = torch.zeros(mt + 1, dtype=torch.int64)
+    rp[1:] = torch.cumsum(torch.bincount(rows, minlength=mt), 0)
+    m, Q, K, V, dO = _tc_backward_case(hd, heads, seq, rp, cols, 90 + hd)
+    Qd, Kd, Vd = (t.cuda().requires_grad_(True) for t in (Q, K, V))
+    ts.block_sparse_attention_tiled(Qd, Kd, Vd, m).backward(dO.cuda())
+    assert ts._lib.device_error() == 0
+    for h in range(heads):
+        args = [t[0, h].float() for t in (Q, K, V)]
+        O = oracle.block_sparse_attention(*args, rp, cols, 128)
+        refs = oracle.block_sparse_attention_backward(*args, O, dO[0, h].float(), rp, cols, 128)
+        for got, ref in zip((Qd.grad, Kd.grad, Vd.grad), refs):
+            assert got.dtype == torch.bfloat16
+            assert rel_fro(got[0, h].float(), ref) <= 2e-2
+    assert torch.count_nonzero(Qd.grad[0, :, 5 * 128:6 * 128]) == 0
+    assert torch.count_nonzero(Kd.grad[0, :, 7 * 128:8 * 128]) == 0
+    assert torch.count_nonzero(Vd.grad[0, :, 7 * 128:8 * 128]) == 0
+
+
+def test_attention_backward_tensor_core_lse_and_cuda_core_agree():
+    """The tensor-core backward with the forward's saved log-sum-exp, with the
+    log-sum-exp recomputed (lse=None) and the CUDA-core backward agree
+    (bf16 outputs, 1e-2 relative Frobenius)."""
+    from trnsparse_b200 import ops
+
+    seq, hd = 128 * 12, 128
+    mask = w.sliding_window_mask(seq=seq, window=4, n_global=1)
+    Q, K, V = (t.cuda() for t in w.attention_inputs(heads=3, seq=seq, hd=hd, seed=61))
+    dO = torch.randn(Q.shape, generator=torch.Generator().manual_seed(62)).to(torch.bfloat16).cuda()
+    scale = 0.11
+    O, lse = ops._attn_forward(Q, K, V, mask, scale, want_lse=True)
+    assert lse is not None and lse.shape == (3 * seq,)
+    a = ops._attn_backward(Q, K, V, O, dO, mask, scale, lse=lse)
+    b = ops._attn_backward(Q, K, V, O, dO, mask, scale, lse=None)
+    c = ops._attn_backward(Q, K, V, O, dO, mask, scale, cuda_cores=True)
+    assert ts._lib.device_error() == 0
+    for x, y, z in zip(a, b, c):
+        assert rel_fro(x.float(), y.float()) <= 1e-2
+        assert rel_fro(x.float(), z.float()) <= 1e-2

@@ -107,3 +107,54 @@ def test_spmm_tc_plan_rejects_small_buffer():
                                                ctypes.c_void_p(plan.data_ptr()), 4, ctypes.byref(nu),
                                                ctypes.byref(grid), ctypes.byref(zero))
     assert rc == _lib.ERR_ARG
+
+
+def test_attention_backward_tc_plan():
+    """Host plan of the tensor-core attention backward (no GPU): per mode every
+    stored (fixed, partner) pair is in exactly one unit, units hold at most
+    `split` partners and come longest first, a fixed block with more partners
+    than `split` gets one workspace slot shared by its units (and an aux
+    entry), and blocks with no partner get a zero-fill aux entry."""
+    import random
+
+    import torch
+
+    rng = random.Random(11)
+    for n, split in [(20, 16), (20, 3), (7, 1), (33, 5)]:
+        keep = [[j <= i and (i - j < 3 or j < 2) and rng.random() > 0.1 for j in range(n)] for i in range(n)]
+        keep[n // 2] = [False] * n
+        rp = [0]
+        for i in range(n):
+            rp.append(rp[-1] + sum(keep[i]))
+        cp = [0]
+        for j in range(n):
+            cp.append(cp[-1] + sum(keep[i][j] for i in range(n)))
+        rp_t, cp_t = torch.tensor(rp, dtype=torch.int32), torch.tensor(cp, dtype=torch.int32)
+        counts = (ctypes.c_int64 * 4)()
+        args = (n, n, ctypes.c_void_p(rp_t.data_ptr()), ctypes.c_void_p(cp_t.data_ptr()), split)
+        assert _lib.load().trnsparse_bsr_attention_backward_tc_plan(*args, None, 0, counts) == _lib.OK
+        total = 4 * (counts[0] + counts[1] + counts[2])
+        plan = torch.zeros(total, dtype=torch.int32)
+        assert _lib.load().trnsparse_bsr_attention_backward_tc_plan(
+            *args, ctypes.c_void_p(plan.data_ptr()), total, counts) == _lib.OK
+        units = plan.view(-1, 4).tolist()
+        ru, cu, aux = units[:counts[0]], units[counts[0]:counts[0] + counts[1]], units[counts[0] + counts[1]:]
+        slots_used = set()
+        for mode, ptr, us in ((0, rp, ru), (1, cp, cu)):
+            covered = {}
+            lengths = [u[2] - u[1] for u in us]
+            assert lengths == sorted(lengths, reverse=True)
+            for f, b0, b1, slot in us:
+                assert ptr[f] <= b0 < b1 <= ptr[f + 1] and b1 - b0 <= split
+                long = ptr[f + 1] - ptr[f] > split
+                assert (slot >= 0) == long
+                if long:
+                    assert [mode, f, slot, 0] in aux
+                    slots_used.add(slot)
+                for e in range(b0, b1):
+                    covered[e] = covered.get(e, 0) + 1
+            assert covered == {e: 1 for e in range(ptr[-1])}
+            for f in range(n):
+                if ptr[f + 1] == ptr[f]:
+                    assert [mode, f, -1, 0] in aux
+        assert slots_used == set(range(counts[3]))

@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
                const int* __restrict__ row_ptr, const int* __restrict__ col_idx, __nv_bfloat16* __restrict__ O,
-               int seq, int m_tiles, int n_tiles, float scale) {
+               float* __restrict__ lse, int seq, int m_tiles, int n_tiles, float scale) {
   using Lay = AtLayout<HD>;
   // No static shared memory: the dynamic window then starts 1024-byte aligned, which the
   // 128-byte-swizzled tiles need (checked below; a misaligned base aborts with an error record).
@@ -405,6 +405,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       const float inv = ok ? 1.f / fmaxf(l_row + l_other, 1e-12f) : 0.f;
+      // base-2 log-sum-exp of the row (scores in s * scale * log2(e) units) for the backward
+      if (lse != nullptr && half == 0 && ok) lse[static_cast<int64_t>(head) * seq + qb * 128 + r] = m + log2f(l_row + l_other);
       if (lr == 0) bulk_wait_read_all();  // the previous tile's store has left the staging slice
       __syncwarp();
 #pragma unroll 1
@@ -449,8 +451,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 }
 
 template <int HD>
-int launch_attn_tc(const void* Q, const void* K, const void* V, void* O, const int* rp, const int* ci, int heads,
-                   int seq, float scale, cudaStream_t st) {
+int launch_attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, const int* rp, const int* ci,
+                   int heads, int seq, float scale, cudaStream_t st) {
   using Lay = AtLayout<HD>;
   const uint64_t rows = static_cast<uint64_t>(heads) * seq;
   CUtensorMap tq, tk, tv, to;
@@ -471,7 +473,8 @@ int launch_attn_tc(const void* Q, const void* K, const void* V, void* O, const i
   const int m_tiles = seq / 128;
   const int n_tiles = m_tiles * heads;
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
-  kern<<<grid, kAtThreads, Lay::kSmem, st>>>(tq, tk, tv, to, rp, ci, (__nv_bfloat16*)O, seq, m_tiles, n_tiles, scale);
+  kern<<<grid, kAtThreads, Lay::kSmem, st>>>(tq, tk, tv, to, rp, ci, (__nv_bfloat16*)O, lse, seq, m_tiles, n_tiles,
+                                                scale);
   TSB_CHECK_LAUNCH("attention_tc launch");
   return debug_sync(st, "attention_tc (sync)");
 }
@@ -481,9 +484,10 @@ int launch_attn_tc(const void* Q, const void* K, const void* V, void* O, const i
 
 using namespace tsb;
 
-extern "C" int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t head_dim, const int* block_row_ptr,
-                                          const int* block_col_idx, const void* Q, const void* K, const void* V,
-                                          void* O, double scale, void* stream) {
+extern "C" int trnsparse_bsr_attention_tc_lse(int64_t heads, int64_t seq, int64_t head_dim,
+                                              const int* block_row_ptr, const int* block_col_idx, const void* Q,
+                                              const void* K, const void* V, void* O, float* lse, double scale,
+                                              void* stream) {
   TSB_REQUIRE(heads > 0 && seq > 0 && seq % 128 == 0 && heads < 65536 && heads * seq < (1ll << 31),
               "attention_tc: needs seq %% 128 == 0 (got heads=%lld seq=%lld)", (long long)heads, (long long)seq);
   TSB_REQUIRE(head_dim == 64 || head_dim == 128, "attention_tc: head_dim must be 64 or 128 (got %lld)",
@@ -491,8 +495,15 @@ extern "C" int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t he
   TSB_REQUIRE(Q && K && V && O && block_row_ptr && block_col_idx, "attention_tc: null pointer");
   cudaStream_t st = as_stream(stream);
   if (head_dim == 64)
-    return launch_attn_tc<64>(Q, K, V, O, block_row_ptr, block_col_idx, (int)heads, (int)seq, (float)scale, st);
-  return launch_attn_tc<128>(Q, K, V, O, block_row_ptr, block_col_idx, (int)heads, (int)seq, (float)scale, st);
+    return launch_attn_tc<64>(Q, K, V, O, lse, block_row_ptr, block_col_idx, (int)heads, (int)seq, (float)scale, st);
+  return launch_attn_tc<128>(Q, K, V, O, lse, block_row_ptr, block_col_idx, (int)heads, (int)seq, (float)scale, st);
+}
+
+extern "C" int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t head_dim, const int* block_row_ptr,
+                                          const int* block_col_idx, const void* Q, const void* K, const void* V,
+                                          void* O, double scale, void* stream) {
+  return trnsparse_bsr_attention_tc_lse(heads, seq, head_dim, block_row_ptr, block_col_idx, Q, K, V, O, nullptr,
+                                        scale, stream);
 }
 
 #ifdef TSB_TC_TRACE

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 
 import torch
 
@@ -569,12 +570,18 @@ def _screened_impl(A: torch.Tensor, diag_integrals: torch.Tensor, B: torch.Tenso
 # ---------------------------------------------------------------------------
 
 
-def _attn_forward(Q, K, V, mask_bsr, scale, cuda_cores: bool = False):
+def _attn_tc_ok(dtype, b, seq, hd, heads) -> bool:
+    """Shapes the tensor-core attention kernels (forward and backward) take."""
+    return dtype == torch.bfloat16 and b == 128 and hd in (64, 128) and seq % 128 == 0 and heads > 0
+
+
+def _attn_forward(Q, K, V, mask_bsr, scale, cuda_cores: bool = False, want_lse: bool = False):
     """Device forward for (S, D) or (..., S, D) inputs sharing one mask.
 
     bf16 with block size 128, head_dim 64/128 and seq a multiple of 128 runs
     the tensor-core kernel; everything else (and ``cuda_cores=True``) runs
-    the CUDA-core kernel."""
+    the CUDA-core kernel. ``want_lse``: return ``(O, lse)`` with the rows'
+    base-2 log-sum-exp from the tensor-core kernel (None otherwise)."""
     seq, hd = Q.shape[-2], Q.shape[-1]
     if Q.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"block_sparse_attention_tiled: dtype {Q.dtype} not supported (float32, bfloat16)")
@@ -592,16 +599,19 @@ def _attn_forward(Q, K, V, mask_bsr, scale, cuda_cores: bool = False):
     heads = Qd.numel() // (seq * hd) if seq * hd else 0
     O = torch.empty_like(Qd)
     code = _lib.F32 if Q.dtype == torch.float32 else _lib.BF16
-    tc = (not cuda_cores and Q.dtype == torch.bfloat16 and b == 128 and hd in (64, 128) and seq % 128 == 0
-          and heads > 0)
+    tc = not cuda_cores and _attn_tc_ok(Q.dtype, b, seq, hd, heads)
+    lse = None
     with torch.cuda.device(dev):
         if tc:
-            _lib.call("trnsparse_bsr_attention_tc", heads, seq, hd, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
-                      Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), float(scale), _lib.stream_handle(dev))
-            return O
-        _lib.call("trnsparse_bsr_attention", heads, seq, hd, b, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
-                  Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), code, float(scale), _lib.stream_handle(dev))
-    return O
+            if want_lse:
+                lse = torch.empty(heads * seq, dtype=torch.float32, device=dev)
+            _lib.call("trnsparse_bsr_attention_tc_lse", heads, seq, hd, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
+                      Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), lse.data_ptr() if lse is not None else None,
+                      float(scale), _lib.stream_handle(dev))
+        else:
+            _lib.call("trnsparse_bsr_attention", heads, seq, hd, b, rp.data_ptr(), ci.data_ptr(), Qd.data_ptr(),
+                      Kd.data_ptr(), Vd.data_ptr(), O.data_ptr(), code, float(scale), _lib.stream_handle(dev))
+    return (O, lse) if want_lse else O
 
 
 def _attn_dense_mask(mask_bsr, seq, dev):
@@ -638,9 +648,36 @@ def _mask_indices(mask_bsr, dev):
     return out
 
 
-def _attn_backward(Q, K, V, O, dO, mask_bsr, scale):
-    """Device backward (reference: ops.py:360-473): stats, dQ (row-first) and
-    dK/dV (column-first over the transposed mask pattern) kernels."""
+_ATTN_BWD_SPLIT = int(os.environ.get("TRNSPARSE_ATTN_BWD_SPLIT", "16"))
+
+
+def _attn_bwd_plan(mask_bsr, dev, rp, cp):
+    """Host-built unit plan of the tensor-core backward (row units, column
+    units, aux entries), cached with the mask's device layout."""
+    lay = mask_bsr.device_layout(dev) if hasattr(mask_bsr, "device_layout") else {}
+    key = ("attn_bwd_plan", _ATTN_BWD_SPLIT)
+    hit = lay.get(key) if lay is not None else None
+    if hit is not None:
+        return hit
+    rp_h = rp.cpu().contiguous()
+    cp_h = cp.cpu().contiguous()
+    counts = (ctypes.c_int64 * 4)()
+    args = (rp_h.numel() - 1, cp_h.numel() - 1, rp_h.data_ptr(), cp_h.data_ptr(), _ATTN_BWD_SPLIT)
+    _lib.call("trnsparse_bsr_attention_backward_tc_plan", *args, None, 0, counts)
+    n = 4 * (counts[0] + counts[1] + counts[2])
+    plan = torch.zeros(max(n, 4), dtype=torch.int32)
+    _lib.call("trnsparse_bsr_attention_backward_tc_plan", *args, plan.data_ptr(), plan.numel(), counts)
+    out = (plan.to(dev), tuple(int(c) for c in counts))
+    if lay is not None and hasattr(mask_bsr, "device_layout"):
+        lay[key] = out
+    return out
+
+
+def _attn_backward(Q, K, V, O, dO, mask_bsr, scale, lse=None, cuda_cores: bool = False):
+    """Device backward (reference: ops.py:360-473). bf16 shapes the tensor
+    cores take run the tcgen05 kernels (dQ row-first, dK/dV column-first,
+    with the forward's log-sum-exp ``lse`` when given); everything else (and
+    ``cuda_cores=True``) runs the CUDA-core stats, dQ and dK/dV kernels."""
     seq, hd = Q.shape[-2], Q.shape[-1]
     dev = Q.device
     rp, ci, cp, ri, max_col = _mask_indices(mask_bsr, dev)
@@ -648,6 +685,17 @@ def _attn_backward(Q, K, V, O, dO, mask_bsr, scale):
     Qd, Kd, Vd, Od, dOd = (t.to(device=dev, dtype=Q.dtype).contiguous() for t in (Q, K, V, O, dO))
     heads = Qd.numel() // (seq * hd) if seq * hd else 0
     dQ, dK, dV = torch.empty_like(Qd), torch.empty_like(Kd), torch.empty_like(Vd)
+    if not cuda_cores and _attn_tc_ok(Q.dtype, b, seq, hd, heads) and rp.numel() - 1 == seq // b and cp.numel() - 1 == seq // b:
+        plan, (n_ru, n_cu, n_aux, n_slots) = _attn_bwd_plan(mask_bsr, dev, rp, cp)
+        ws_bytes = _lib.raw("trnsparse_bsr_attention_backward_tc_workspace_size")(heads, seq, hd, n_slots)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("trnsparse_bsr_attention_backward_tc", heads, seq, hd, rp.data_ptr(), ci.data_ptr(),
+                      ri.data_ptr(), plan.data_ptr(), n_ru, n_cu, n_aux, n_slots, Qd.data_ptr(), Kd.data_ptr(),
+                      Vd.data_ptr(), Od.data_ptr(), dOd.data_ptr(), lse.data_ptr() if lse is not None else None,
+                      dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), float(scale), ws.data_ptr(), ws_bytes,
+                      _lib.stream_handle(dev))
+        return dQ, dK, dV
     code = _lib.F32 if Q.dtype == torch.float32 else _lib.BF16
     ws_bytes = _lib.raw("trnsparse_bsr_attention_backward_workspace_size")(heads, seq, hd, code, max_col)
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
@@ -666,15 +714,15 @@ class _AttnFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, Q, K, V, mask_bsr, scale):
-        O = _attn_forward(Q, K, V, mask_bsr, scale)
-        ctx.save_for_backward(Q, K, V, O)
+        O, lse = _attn_forward(Q, K, V, mask_bsr, scale, want_lse=True)
+        ctx.save_for_backward(Q, K, V, O, lse)
         ctx.mask_bsr, ctx.scale = mask_bsr, scale
         return O
 
     @staticmethod
     def backward(ctx, dO):
-        Q, K, V, O = ctx.saved_tensors
-        dQ, dK, dV = _attn_backward(Q, K, V, O, dO, ctx.mask_bsr, ctx.scale)
+        Q, K, V, O, lse = ctx.saved_tensors
+        dQ, dK, dV = _attn_backward(Q, K, V, O, dO, ctx.mask_bsr, ctx.scale, lse=lse)
         return dQ.view_as(Q), dK.view_as(K), dV.view_as(V), None, None
 
 
