@@ -15,17 +15,18 @@
 //   column mode (dK, dV) fixed K, V of a key block; streamed Q, dO (and the
 //                     lse / D of their rows) of the query blocks that store
 //                     it (block_row_idx of the transposed pattern).
-// Per partner block the MMA warp issues S = F1 X1^T and dP = F2 X2^T
-// (128x128, K = head_dim) into TMEM columns [0,128) and [128,256); eight
-// warps read them (one TMEM lane = one fixed row per thread, 64 columns per
-// warp half), form P and dS in fp32 and write them back as packed bf16 into
-// the columns they just read; the MMA warp then adds dS X1 (and, in column
-// mode, P X2) into the TMEM accumulators at column 256 (+ head_dim) with A
-// taken from TMEM and the streamed tile as an MN-major B. At the end of a
-// unit the same eight warps scale the accumulators, stage them as bf16 in the
-// fixed tiles' shared memory and write them with TMA stores; units of a
-// block that was split over several CTAs add fp32 partial sums into a
-// workspace slot instead, converted by a finishing kernel.
+// Per partner block the MMA warp issues S = F1 X1^T, then dP = F2 X2^T
+// (128x128, K = head_dim) into the same 128 TMEM columns; eight warps read
+// them (one TMEM lane = one fixed row per thread, 64 columns per warp half),
+// form P and dS in fp32 and write them as packed bf16 into two 64-column
+// TMEM areas; the MMA warp adds dS X1 (and, in column mode, P X2) into the
+// TMEM accumulators at column 256 (+ head_dim) with A taken from TMEM and
+// the streamed tile as an MN-major B. The score columns are released as soon
+// as they are read, so the next block's S runs on the tensor core while the
+// warps compute this block's dS. At the end of a unit the same eight warps
+// scale the accumulators and store them as bf16 rows; units of a block that
+// was split over several CTAs add fp32 partial sums into a workspace slot
+// instead, converted by a finishing kernel.
 //
 // Warps: 0-7 dS / epilogue, 8 TMA producer, 9 TMEM owner and MMA issuer.
 // Every wait is bounded (ptx.cuh): a stalled partner ends in an error record.
@@ -44,6 +45,10 @@ extern "C" int trnsparse_bsr_attention_tc_lse(int64_t heads, int64_t seq, int64_
 namespace tsb {
 namespace {
 
+#ifndef TSB_AB_X1_STAGES
+#define TSB_AB_X1_STAGES 2
+#endif
+
 constexpr int kAbEpi = 256;               // dS / epilogue threads (warps 0-7)
 constexpr int kAbThreads = kAbEpi + 64;   // + producer warp + MMA warp
 
@@ -51,23 +56,41 @@ template <int HD>
 struct AbLayout {
   static constexpr int kChunks = HD / 64;       // 128-byte column chunks of a row
   static constexpr int kTile = 128 * HD * 2;    // one 128-row bf16 tile
-  static constexpr int kF1 = 0, kF2 = kTile;    // fixed tiles (also the output staging)
-  static constexpr int kX = 2 * kTile;          // streamed stages: X1, X2, lse[128], D[128]
-  static constexpr int kStage = 2 * kTile + 1024;
-  static constexpr int kStages = 2;
-  static constexpr int kBar = kX + kStages * kStage;
+  static constexpr int kF1 = 0, kF2 = kTile;    // fixed tiles
+  // streamed tiles: X1 (used by S and by the dS product) and X2 (used by dP and, in column
+  // mode, the P product; with the partner rows' lse[128], D[128]) in separate rings, released
+  // at different times (a third X1 stage, which fits, measured no faster: the loads are bound
+  // by the rate tiles arrive from L2, not by how early they are issued)
+  static constexpr int kX1 = 2 * kTile, kX1Stages = TSB_AB_X1_STAGES;
+  static constexpr int kX2 = kX1 + kX1Stages * kTile, kX2Stage = kTile + 1024, kX2Stages = 2;
+  static constexpr int kBar = kX2 + kX2Stages * kX2Stage;
   static constexpr int kSmem = kBar + 256;
-  static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemAcc = 256;  // accumulators at 256 (+HD)
+  // TMEM: S, then dP, in [0,128); P and dS as packed bf16 in [128,192) and [192,256);
+  // accumulators at 256 (dQ, or dK) and 256 + HD (dV)
+  static constexpr uint32_t kTmemA = 0, kTmemP = 128, kTmemDS = 192, kTmemAcc = 256;
   static constexpr int kTmemCols = 512;
 };
 
 struct AbBars {
   uint64_t f_full, f_empty, acc_full, acc_empty;
-  uint64_t x_full[2], x_empty[2];
-  uint64_t s_full, p_full, mma_done;
+  uint64_t x1_full[TSB_AB_X1_STAGES], x1_empty[TSB_AB_X1_STAGES], x2_full[2], x2_empty[2];
+  uint64_t a_full, a_empty, p_full, p_free, ds_full, ds_free;
   uint32_t tmem_slot;
   int abort_flag;
 };
+
+#ifdef TSB_TC_TRACE
+__device__ unsigned long long g_ab_trace[2][10][64];
+// (CTA 64 only) event ev of step i in mode m
+#define AB_TRACE(ev, i)                                                                     \
+  if (blockIdx.x == 64 && (i) < 64) {                                                       \
+    unsigned long long tt_;                                                                 \
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(tt_));                                 \
+    g_ab_trace[COL ? 1 : 0][ev][i] = tt_;                                                   \
+  }
+#else
+#define AB_TRACE(ev, i)
+#endif
 
 __device__ __forceinline__ float ab_ex2(float x) {
   float y;
@@ -75,16 +98,27 @@ __device__ __forceinline__ float ab_ex2(float x) {
   return y;
 }
 
+// TMEM column of the packed A operand (P or dS) for partner rows 16 kk .. 16 kk + 15:
+// warp half h packs partner columns 64 h .. 64 h + 63 into 32 columns.
+__device__ __forceinline__ uint32_t ab_a_col(int kk) { return (kk >> 2) * 32 + (kk & 3) * 8; }
+
 // units: {fixed block, first partner index, end partner index, workspace slot or -1}.
 // Tile t covers unit t / heads of head t % heads (heads of a long unit run side by side).
+//
+// Per partner block j the MMA warp issues, in order: S_j = F1 X1^T into the score columns,
+// the previous block's dS_{j-1} X1 product, dP_j = F2 X2^T into the same columns once S_j
+// has been read, and (column mode) P_j X2 once P_j is written. The eight warps read S_j,
+// release the columns, form P_j (fp32, kept in registers; packed into TMEM in column mode),
+// read dP_j, release the columns and write dS_j = P_j (dP_j - D) packed. So the tensor
+// core works on one block's scores while the warps work on the other's.
 template <int HD, bool COL>
 __global__ void __launch_bounds__(kAbThreads, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tf1, const __grid_constant__ CUtensorMap tf2,
                    const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2,
-                   const __grid_constant__ CUtensorMap to1, const __grid_constant__ CUtensorMap to2,
                    const int4* __restrict__ units, const int* __restrict__ partner, int n_tiles, int heads,
                    int seq, const float* __restrict__ lse2, const float* __restrict__ delta,
-                   float* __restrict__ slots, float scale) {
+                   __nv_bfloat16* __restrict__ out1, __nv_bfloat16* __restrict__ out2, float* __restrict__ slots,
+                   float scale) {
   using Lay = AbLayout<HD>;
   extern __shared__ __align__(16) uint8_t sb[];  // no static smem: the window is 1024-byte aligned
   AbBars& B = *reinterpret_cast<AbBars*>(sb + Lay::kBar);
@@ -92,16 +126,23 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tf1, const __grid_constan
 
   if (threadIdx.x == 0) {
     mbar_init(&B.f_full, 1);
-    mbar_init(&B.f_empty, kAbEpi / 32);
+    mbar_init(&B.f_empty, 1);
     mbar_init(&B.acc_full, 1);
     mbar_init(&B.acc_empty, kAbEpi);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&B.x_full[i], 1);
-      mbar_init(&B.x_empty[i], 1);
+    for (int i = 0; i < TSB_AB_X1_STAGES; ++i) {
+      mbar_init(&B.x1_full[i], 1);
+      mbar_init(&B.x1_empty[i], 1);
     }
-    mbar_init(&B.s_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.x2_full[i], 1);
+      mbar_init(&B.x2_empty[i], 1);
+    }
+    mbar_init(&B.a_full, 1);
+    mbar_init(&B.a_empty, kAbEpi);
     mbar_init(&B.p_full, kAbEpi);
-    mbar_init(&B.mma_done, 1);
+    mbar_init(&B.p_free, 1);
+    mbar_init(&B.ds_full, kAbEpi);
+    mbar_init(&B.ds_free, 1);
     B.abort_flag = (smem_u32(sb) & 1023u) ? 1 : 0;
     if (B.abort_flag) record_device_error(DEVERR_SELFCHECK_SMEM);
     fence_mbar_init();
@@ -117,34 +158,45 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tf1, const __grid_constan
   volatile int* abort_flag = &B.abort_flag;
 
   if (warp == 8) {
-    // ---------------- TMA producer
-    if (elect_lane0() && !*abort_flag) {
+    // ---------------- TMA producers: lane 0 the fixed tiles and X1, lane 1 X2 (and the
+    // partner rows' statistics); the two rings are released at different times
+    const int lane = threadIdx.x & 31;
+    if (lane < 2 && !*abort_flag) {
       int gs = 0, nt = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++nt) {
         const int4 u = units[t / heads];
         const int row0 = (t % heads) * seq;
-        if (nt > 0 && !mbar_wait(&B.f_empty, (nt - 1) & 1)) { ok = false; break; }
-        mbar_arrive_expect_tx(&B.f_full, 2 * Lay::kTile);
-        for (int c = 0; c < Lay::kChunks; ++c) {
-          tma_load_2d(sb + Lay::kF1 + c * 16384, &tf1, c * 64, row0 + u.x * 128, &B.f_full);
-          tma_load_2d(sb + Lay::kF2 + c * 16384, &tf2, c * 64, row0 + u.x * 128, &B.f_full);
+        if (lane == 0) {
+          // the fixed tiles are free once the previous unit's last dP has run
+          if (nt > 0 && !mbar_wait(&B.f_empty, (nt - 1) & 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&B.f_full, 2 * Lay::kTile);
+          for (int c = 0; c < Lay::kChunks; ++c) {
+            tma_load_2d(sb + Lay::kF1 + c * 16384, &tf1, c * 64, row0 + u.x * 128, &B.f_full);
+            tma_load_2d(sb + Lay::kF2 + c * 16384, &tf2, c * 64, row0 + u.x * 128, &B.f_full);
+          }
         }
         for (int e = u.y; e < u.z; ++e, ++gs) {
-          const int st = gs & 1, use = gs >> 1;
-          if (*abort_flag || (use > 0 && !mbar_wait(&B.x_empty[st], (use - 1) & 1))) { ok = false; break; }
           const int pb = partner[e];
           const int xrow = row0 + pb * 128;
-          uint8_t* xs = sb + Lay::kX + st * Lay::kStage;
-          mbar_arrive_expect_tx(&B.x_full[st], 2 * Lay::kTile + (COL ? 1024 : 0));
-          for (int c = 0; c < Lay::kChunks; ++c) {
-            tma_load_2d(xs + c * 16384, &tx1, c * 64, xrow, &B.x_full[st]);
-            tma_load_2d(xs + Lay::kTile + c * 16384, &tx2, c * 64, xrow, &B.x_full[st]);
-          }
-          if (COL) {
-            const int vrow = (pb >= 0 && pb * 128 < seq) ? xrow : row0;  // never read past the statistics
-            bulk_g2s(xs + 2 * Lay::kTile, lse2 + vrow, 512, &B.x_full[st]);
-            bulk_g2s(xs + 2 * Lay::kTile + 512, delta + vrow, 512, &B.x_full[st]);
+          if (lane == 0) {
+            const int st = gs % TSB_AB_X1_STAGES, use = gs / TSB_AB_X1_STAGES;
+            if (*abort_flag || (use > 0 && !mbar_wait(&B.x1_empty[st], (use - 1) & 1))) { ok = false; break; }
+            AB_TRACE(0, gs);
+            uint8_t* xs = sb + Lay::kX1 + st * Lay::kTile;
+            mbar_arrive_expect_tx(&B.x1_full[st], Lay::kTile);
+            for (int c = 0; c < Lay::kChunks; ++c) tma_load_2d(xs + c * 16384, &tx1, c * 64, xrow, &B.x1_full[st]);
+          } else {
+            const int st = gs & 1, use = gs >> 1;
+            if (*abort_flag || (use > 0 && !mbar_wait(&B.x2_empty[st], (use - 1) & 1))) { ok = false; break; }
+            uint8_t* xs = sb + Lay::kX2 + st * Lay::kX2Stage;
+            mbar_arrive_expect_tx(&B.x2_full[st], Lay::kTile + (COL ? 1024 : 0));
+            for (int c = 0; c < Lay::kChunks; ++c) tma_load_2d(xs + c * 16384, &tx2, c * 64, xrow, &B.x2_full[st]);
+            if (COL) {
+              const int vrow = (pb >= 0 && pb * 128 < seq) ? xrow : row0;  // never read past the statistics
+              bulk_g2s(xs + Lay::kTile, lse2 + vrow, 512, &B.x2_full[st]);
+              bulk_g2s(xs + Lay::kTile + 512, delta + vrow, 512, &B.x2_full[st]);
+            }
           }
         }
       }
@@ -156,52 +208,91 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tf1, const __grid_constan
       constexpr uint32_t idesc_s = make_idesc(MmaKind::BF16, 128, 128);
       constexpr uint32_t idesc_a = make_idesc(MmaKind::BF16, 128, HD) | (1u << 16);  // B MN-major
       const uint32_t f1 = smem_u32(sb + Lay::kF1), f2 = smem_u32(sb + Lay::kF2);
-      int gs = 0, nt = 0;
       bool ok = !*abort_flag;
+      // the dS X1 product of the previous partner block, issued after the next block's S
+      bool pend = false, pfirst = false, plast = false;
+      int pgs = 0, pnt = 0;
+      auto issue_ds = [&]() -> bool {
+        if (!mbar_wait(&B.ds_full, pgs & 1)) return false;
+        if (!COL && pfirst && pnt > 0 && !mbar_wait(&B.acc_empty, (pnt - 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t x1 = smem_u32(sb + Lay::kX1 + (pgs % TSB_AB_X1_STAGES) * Lay::kTile);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 128 partner rows, 16 per MMA
+          umma_ts_f16(tmem + Lay::kTmemAcc, tmem + Lay::kTmemDS + ab_a_col(kk),
+                      smem_desc_sw128_mn(x1 + kk * 2048, 16384), idesc_a, !pfirst || kk > 0);
+        umma_commit(&B.ds_free);
+        umma_commit(&B.x1_empty[pgs % TSB_AB_X1_STAGES]);
+        if (COL) umma_commit(&B.x2_empty[pgs & 1]);  // dO, and D read by the dS warps
+        if (plast) umma_commit(&B.acc_full);
+        return true;
+      };
+      int gs = 0, nt = 0;
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++nt) {
         const int4 u = units[t / heads];
+        // close the previous unit (its accumulators go to the epilogue) before waiting for new fixed tiles
+        if (pend && !issue_ds()) { ok = false; break; }
+        pend = false;
         if (!mbar_wait(&B.f_full, nt & 1)) { ok = false; break; }
         for (int e = u.y; e < u.z; ++e, ++gs) {
-          const int st = gs & 1, use = gs >> 1;
-          if (*abort_flag || !mbar_wait(&B.x_full[st], use & 1)) { ok = false; break; }
-          // the previous block's products have read P / dS out of the score columns
-          if (gs > 0 && !mbar_wait(&B.mma_done, (gs - 1) & 1)) { ok = false; break; }
+          const bool first = e == u.y, last = e == u.z - 1;
+          if (*abort_flag || !mbar_wait(&B.x1_full[gs % TSB_AB_X1_STAGES], (gs / TSB_AB_X1_STAGES) & 1)) { ok = false; break; }
+          AB_TRACE(1, gs);
+          // score columns free: the previous block's dP has been read (a_empty completion 2 gs - 1)
+          if (gs > 0 && !mbar_wait(&B.a_empty, 1)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t x1 = smem_u32(sb + Lay::kX + st * Lay::kStage), x2 = x1 + Lay::kTile;
+          const uint32_t x1 = smem_u32(sb + Lay::kX1 + (gs % TSB_AB_X1_STAGES) * Lay::kTile);
+          const uint32_t x2 = smem_u32(sb + Lay::kX2 + (gs & 1) * Lay::kX2Stage);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma<MmaKind::BF16>(tmem + Lay::kTmemS, smem_desc_sw128(f1 + off), smem_desc_sw128(x1 + off), idesc_s,
-                                kk > 0);
-            umma<MmaKind::BF16>(tmem + Lay::kTmemDP, smem_desc_sw128(f2 + off), smem_desc_sw128(x2 + off), idesc_s,
+            umma<MmaKind::BF16>(tmem + Lay::kTmemA, smem_desc_sw128(f1 + off), smem_desc_sw128(x1 + off), idesc_s,
                                 kk > 0);
           }
-          umma_commit(&B.s_full);
-          if (!mbar_wait(&B.p_full, gs & 1)) { ok = false; break; }
-          if (e == u.y && nt > 0 && !mbar_wait(&B.acc_empty, (nt - 1) & 1)) { ok = false; break; }
+          umma_commit(&B.a_full);
+          AB_TRACE(2, gs);
+          if (pend && !issue_ds()) { ok = false; break; }
+          AB_TRACE(3, gs);
+          pend = false;
+          // S read (a_empty completion 2 gs): dP into the same columns
+          if (!mbar_wait(&B.a_empty, 0) || !mbar_wait(&B.x2_full[gs & 1], (gs >> 1) & 1)) { ok = false; break; }
           tc_fence_after();
-          const bool acc = e > u.y;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // 128 partner rows, 16 per MMA (8 packed TMEM columns)
-            const uint32_t a_col = (kk >> 2) * 64 + (kk & 3) * 8;
-            umma_ts_f16(tmem + Lay::kTmemAcc, tmem + Lay::kTmemDP + a_col, smem_desc_sw128_mn(x1 + kk * 2048, 16384),
-                        idesc_a, acc || kk > 0);
-            if (COL)
-              umma_ts_f16(tmem + Lay::kTmemAcc + HD, tmem + Lay::kTmemS + a_col,
-                          smem_desc_sw128_mn(x2 + kk * 2048, 16384), idesc_a, acc || kk > 0);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma<MmaKind::BF16>(tmem + Lay::kTmemA, smem_desc_sw128(f2 + off), smem_desc_sw128(x2 + off), idesc_s,
+                                kk > 0);
           }
-          umma_commit(&B.x_empty[st]);
-          umma_commit(&B.mma_done);
-          if (e == u.z - 1) umma_commit(&B.acc_full);
+          umma_commit(&B.a_full);
+          if (!COL) umma_commit(&B.x2_empty[gs & 1]);  // V is read by dP only
+          AB_TRACE(4, gs);
+          if (last) umma_commit(&B.f_empty);  // the fixed tiles are read for the last time
+          if (COL) {
+            if (!mbar_wait(&B.p_full, gs & 1)) { ok = false; break; }
+            if (first && nt > 0 && !mbar_wait(&B.acc_empty, (nt - 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_ts_f16(tmem + Lay::kTmemAcc + HD, tmem + Lay::kTmemP + ab_a_col(kk),
+                          smem_desc_sw128_mn(x2 + kk * 2048, 16384), idesc_a, !first || kk > 0);
+            umma_commit(&B.p_free);
+          }
+          pend = true;
+          pgs = gs;
+          pnt = nt;
+          pfirst = first;
+          plast = last;
         }
       }
+      if (ok && pend && !issue_ds()) ok = false;
       if (!ok) atomicExch(&B.abort_flag, 1);
     }
   } else {
-    // ---------------- dS and epilogue warps
+    // ---------------- P / dS and epilogue warps
     const int quad = warp & 3, half = warp >> 2, lr = threadIdx.x & 31;
     const int r = quad * 32 + lr;  // fixed row of this thread (TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tl = tmem + lane_base;
     const float sl = scale * 1.4426950408889634f;
     int gs = 0, nt = 0;
     bool ok = !*abort_flag;
@@ -215,58 +306,114 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tf1, const __grid_constan
         d_r = delta[frow];
       }
       for (int e = u.y; e < u.z; ++e, ++gs) {
-        const int st = gs & 1;
-        if (*abort_flag || !mbar_wait(&B.s_full, gs & 1)) { ok = false; break; }
-        const float* vl = reinterpret_cast<const float*>(sb + Lay::kX + st * Lay::kStage + 2 * Lay::kTile);
-        if (COL && !mbar_wait(&B.x_full[st], (gs >> 1) & 1)) { ok = false; break; }  // lse / D of the partner rows
+        const float4* vl4 =
+            reinterpret_cast<const float4*>(sb + Lay::kX2 + (gs & 1) * Lay::kX2Stage + Lay::kTile) + half * 16;
+        if (*abort_flag || (COL && !mbar_wait(&B.x2_full[gs & 1], (gs >> 1) & 1))) { ok = false; break; }
+        // ---- S -> P
+        if (!mbar_wait(&B.a_full, 0)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t col = half * 64 + c * 32;
-          uint32_t s[32], dp[32];
-          tmem_ld32(tmem + lane_base + Lay::kTmemS + col, s);
-          tmem_ld32(tmem + lane_base + Lay::kTmemDP + col, dp);
+        float p[64];
+        {
+          uint32_t v0[32], v1[32];
+          tmem_ld32(tl + Lay::kTmemA + half * 64, v0);
+          tmem_ld32(tl + Lay::kTmemA + half * 64 + 32, v1);
           tmem_wait_ld();
-          uint32_t pp[16], pd[16];
+          tc_fence_before();
+          mbar_arrive(&B.a_empty);
+          if (threadIdx.x == 0) AB_TRACE(5, gs);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float l0 = l_r, l1 = l_r, d0 = d_r, d1 = d_r;
-            if (COL) {
-              l0 = vl[col + i];
-              l1 = vl[col + i + 1];
-              d0 = vl[128 + col + i];
-              d1 = vl[128 + col + i + 1];
-            }
-            const float p0 = ab_ex2(fmaf(__uint_as_float(s[i]), sl, -l0));
-            const float p1 = ab_ex2(fmaf(__uint_as_float(s[i + 1]), sl, -l1));
-            pp[i / 2] = pack_bf16(p0, p1);
-            pd[i / 2] = pack_bf16(p0 * (__uint_as_float(dp[i]) - d0), p1 * (__uint_as_float(dp[i + 1]) - d1));
+          for (int i = 0; i < 32; ++i) {
+            p[i] = __uint_as_float(v0[i]);
+            p[32 + i] = __uint_as_float(v1[i]);
           }
-          // packed bf16 back into the columns just read: A operands of the products
-          if (COL) tmem_st16(tmem + lane_base + Lay::kTmemS + half * 64 + c * 16, pp);
-          tmem_st16(tmem + lane_base + Lay::kTmemDP + half * 64 + c * 16, pd);
         }
+        if (COL) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float4 l4 = vl4[i];
+            p[4 * i] = ab_ex2(fmaf(p[4 * i], sl, -l4.x));
+            p[4 * i + 1] = ab_ex2(fmaf(p[4 * i + 1], sl, -l4.y));
+            p[4 * i + 2] = ab_ex2(fmaf(p[4 * i + 2], sl, -l4.z));
+            p[4 * i + 3] = ab_ex2(fmaf(p[4 * i + 3], sl, -l4.w));
+          }
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16(p[2 * i], p[2 * i + 1]);
+          if (gs > 0 && !mbar_wait(&B.p_free, (gs - 1) & 1)) { ok = false; break; }
+          tc_fence_after();
+          tmem_st32(tl + Lay::kTmemP + half * 32, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&B.p_full);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) p[i] = ab_ex2(fmaf(p[i], sl, -l_r));
+        }
+        // ---- dP -> dS = P (dP - D)
+        if (threadIdx.x == 0) AB_TRACE(6, gs);
+        if (!mbar_wait(&B.a_full, 1)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t pk[32];
+        {
+          uint32_t v0[32], v1[32];
+          tmem_ld32(tl + Lay::kTmemA + half * 64, v0);
+          tmem_ld32(tl + Lay::kTmemA + half * 64 + 32, v1);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(&B.a_empty);
+          if (threadIdx.x == 0) AB_TRACE(7, gs);
+          if (COL) {
+            const float4* d4 = vl4 + 32;  // D follows the 128 lse values
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 a = d4[i], b = d4[8 + i];
+              pk[2 * i] = pack_bf16(p[4 * i] * (__uint_as_float(v0[4 * i]) - a.x),
+                                    p[4 * i + 1] * (__uint_as_float(v0[4 * i + 1]) - a.y));
+              pk[2 * i + 1] = pack_bf16(p[4 * i + 2] * (__uint_as_float(v0[4 * i + 2]) - a.z),
+                                        p[4 * i + 3] * (__uint_as_float(v0[4 * i + 3]) - a.w));
+              pk[16 + 2 * i] = pack_bf16(p[32 + 4 * i] * (__uint_as_float(v1[4 * i]) - b.x),
+                                         p[32 + 4 * i + 1] * (__uint_as_float(v1[4 * i + 1]) - b.y));
+              pk[16 + 2 * i + 1] = pack_bf16(p[32 + 4 * i + 2] * (__uint_as_float(v1[4 * i + 2]) - b.z),
+                                             p[32 + 4 * i + 3] * (__uint_as_float(v1[4 * i + 3]) - b.w));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              pk[i] = pack_bf16(p[2 * i] * (__uint_as_float(v0[2 * i]) - d_r),
+                                p[2 * i + 1] * (__uint_as_float(v0[2 * i + 1]) - d_r));
+              pk[16 + i] = pack_bf16(p[32 + 2 * i] * (__uint_as_float(v1[2 * i]) - d_r),
+                                     p[32 + 2 * i + 1] * (__uint_as_float(v1[2 * i + 1]) - d_r));
+            }
+          }
+        }
+        if (gs > 0 && !mbar_wait(&B.ds_free, (gs - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st32(tl + Lay::kTmemDS + half * 32, pk);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&B.p_full);
+        mbar_arrive(&B.ds_full);
+        if (threadIdx.x == 0) AB_TRACE(8, gs);
       }
       if (!ok) break;
-      // ---- unit epilogue: accumulators -> bf16 staging in the fixed tiles -> TMA stores
+      // ---- unit epilogue: accumulators (x scale for dQ / dK) -> bf16 rows, or fp32 partial sums
       if (!mbar_wait(&B.acc_full, nt & 1)) { ok = false; break; }
+      if (threadIdx.x == 0) AB_TRACE(9, nt);
       tc_fence_after();
       const int slot = u.w;
+      const bool live = u.x * 128 + r < seq;
 #pragma unroll 1
       for (int a = 0; a < (COL ? 2 : 1); ++a) {
         const float mul = a == 0 ? scale : 1.f;
-        uint8_t* const stage = sb + (a == 0 ? Lay::kF1 : Lay::kF2) + half * (Lay::kTile / 2) + quad * (Lay::kTile / 8);
-        float* const wrow =
-            slot >= 0 ? slots + ((static_cast<int64_t>(slot) * heads + head) * 2 + a) * 128 * HD + r * HD + half * (HD / 2)
-                      : nullptr;
+        float* const wrow = slot >= 0 ? slots + ((static_cast<int64_t>(slot) * heads + head) * 2 + a) * 128 * HD +
+                                            r * HD + half * (HD / 2)
+                                      : nullptr;
+        __nv_bfloat16* const orow = (a == 0 ? out1 : out2) + frow * HD + half * (HD / 2);
 #pragma unroll 1
         for (int c = 0; c < HD / 64; ++c) {
           uint32_t v[32];
-          tmem_ld32(tmem + lane_base + Lay::kTmemAcc + a * HD + half * (HD / 2) + c * 32, v);
+          tmem_ld32(tl + Lay::kTmemAcc + a * HD + half * (HD / 2) + c * 32, v);
           tmem_wait_ld();
+          if (!live) continue;
           if (slot >= 0) {
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -275,38 +422,20 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tf1, const __grid_constan
                          __float_as_uint(__uint_as_float(v[4 * q + 2]) * mul),
                          __float_as_uint(__uint_as_float(v[4 * q + 3]) * mul));
           } else {
+            uint4* o4 = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               auto f = [&](int i) { return __uint_as_float(v[8 * q + i]) * mul; };
-              const int unit = c * 4 + q;  // 16-byte unit of the staged row
-              const int pos =
-                  HD == 128 ? (unit ^ (lr & 7)) * 16 + lr * 128 : (unit ^ ((lr >> 1) & 3)) * 16 + lr * 64;
-              *reinterpret_cast<uint4*>(stage + pos) = make_uint4(pack_bf16(f(0), f(1)), pack_bf16(f(2), f(3)),
-                                                                 pack_bf16(f(4), f(5)), pack_bf16(f(6), f(7)));
+              o4[q] = make_uint4(pack_bf16(f(0), f(1)), pack_bf16(f(2), f(3)), pack_bf16(f(4), f(5)),
+                                 pack_bf16(f(6), f(7)));
             }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&B.acc_empty);  // accumulators read: the next unit's products may start
-      if (slot < 0) {
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lr == 0) {
-          const int orow = head * seq + u.x * 128 + quad * 32;
-          tma_store_2d(&to1, sb + Lay::kF1 + half * (Lay::kTile / 2) + quad * (Lay::kTile / 8), half * (HD / 2), orow);
-          if (COL)
-            tma_store_2d(&to2, sb + Lay::kF2 + half * (Lay::kTile / 2) + quad * (Lay::kTile / 8), half * (HD / 2),
-                         orow);
-          bulk_commit_group();
-          bulk_wait_read_all();  // staging (the fixed tiles) may be refilled
-        }
-      }
-      __syncwarp();
-      if (lr == 0) mbar_arrive(&B.f_empty);
     }
     if (!ok) atomicExch(&B.abort_flag, 1);
-    if (lr == 0) bulk_wait_all();
   }
   __syncwarp();
   tc_fence_before();
@@ -370,7 +499,8 @@ __global__ void attn_bwd_aux_kernel(const int4* __restrict__ aux, int heads, int
 
 template <int HD, bool COL>
 int launch_ab_mode(const CUtensorMap* maps, const int4* units, int n_units, const int* partner, int heads, int seq,
-                   const float* lse2, const float* delta, float* slots, float scale, cudaStream_t st) {
+                   const float* lse2, const float* delta, void* out1, void* out2, float* slots, float scale,
+                   cudaStream_t st) {
   if (n_units <= 0) return TRNSPARSE_OK;
   using Lay = AbLayout<HD>;
   auto kern = attn_bwd_tc_kernel<HD, COL>;
@@ -378,13 +508,15 @@ int launch_ab_mode(const CUtensorMap* maps, const int4* units, int n_units, cons
   if (e != cudaSuccess) return cuda_status(e, "attention_backward_tc: set smem");
   const int64_t n_tiles = static_cast<int64_t>(n_units) * heads;
   const int grid = n_tiles < sm_count() ? (int)n_tiles : sm_count();
-  // maps: 0 Q, 1 K, 2 V, 3 dO, 4 dQ, 5 dK, 6 dV
+  // maps: 0 Q, 1 K, 2 V, 3 dO
   if (COL)
-    kern<<<grid, kAbThreads, Lay::kSmem, st>>>(maps[1], maps[2], maps[0], maps[3], maps[5], maps[6], units, partner,
-                                               (int)n_tiles, heads, seq, lse2, delta, slots, scale);
+    kern<<<grid, kAbThreads, Lay::kSmem, st>>>(maps[1], maps[2], maps[0], maps[3], units, partner, (int)n_tiles,
+                                               heads, seq, lse2, delta, (__nv_bfloat16*)out1, (__nv_bfloat16*)out2,
+                                               slots, scale);
   else
-    kern<<<grid, kAbThreads, Lay::kSmem, st>>>(maps[0], maps[3], maps[1], maps[2], maps[4], maps[4], units, partner,
-                                               (int)n_tiles, heads, seq, lse2, delta, slots, scale);
+    kern<<<grid, kAbThreads, Lay::kSmem, st>>>(maps[0], maps[3], maps[1], maps[2], units, partner, (int)n_tiles,
+                                               heads, seq, lse2, delta, (__nv_bfloat16*)out1, (__nv_bfloat16*)out1,
+                                               slots, scale);
   TSB_CHECK_LAUNCH(COL ? "attention_backward_tc: dK dV" : "attention_backward_tc: dQ");
   return debug_sync(st, COL ? "attention_backward_tc: dK dV (sync)" : "attention_backward_tc: dQ (sync)");
 }
@@ -410,13 +542,10 @@ int launch_ab(int heads, int seq, const int* rp, const int* ci, const int* ri, c
   } else {
     lse2 = const_cast<float*>(lse_in);
   }
-  CUtensorMap maps[7];
-  const void* bases[7] = {Q, K, V, dO, dQ, dK, dV};
-  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  for (int i = 0; i < 7; ++i) {
-    int rc = i < 4 ? make_tmap_2d(&maps[i], bases[i], dt, HD, rows, HD * 2, 64, 128)
-                   : make_tmap_2d(&maps[i], bases[i], dt, HD, rows, HD * 2, HD / 2, 32,
-                                  HD == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  CUtensorMap maps[4];
+  const void* bases[4] = {Q, K, V, dO};
+  for (int i = 0; i < 4; ++i) {
+    int rc = make_tmap_2d(&maps[i], bases[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, HD, rows, HD * 2, 64, 128);
     if (rc) return rc;
   }
   const int4* aux = plan + n_row_units + n_col_units;
@@ -425,9 +554,10 @@ int launch_ab(int heads, int seq, const int* rp, const int* ci, const int* ri, c
                                                                      (__nv_bfloat16*)dK, (__nv_bfloat16*)dV);
     TSB_CHECK_LAUNCH("attention_backward_tc: zero slots");
   }
-  int rc = launch_ab_mode<HD, false>(maps, plan, n_row_units, ci, heads, seq, lse2, delta, slots, scale, st);
+  int rc = launch_ab_mode<HD, false>(maps, plan, n_row_units, ci, heads, seq, lse2, delta, dQ, dQ, slots, scale, st);
   if (rc) return rc;
-  rc = launch_ab_mode<HD, true>(maps, plan + n_row_units, n_col_units, ri, heads, seq, lse2, delta, slots, scale, st);
+  rc = launch_ab_mode<HD, true>(maps, plan + n_row_units, n_col_units, ri, heads, seq, lse2, delta, dK, dV, slots,
+                                scale, st);
   if (rc) return rc;
   if (n_aux > 0) {
     attn_bwd_aux_kernel<HD, false><<<dim3(n_aux, heads), 256, 0, st>>>(aux, heads, seq, slots, (__nv_bfloat16*)dQ,
@@ -539,3 +669,9 @@ extern "C" int trnsparse_bsr_attention_backward_tc(int64_t heads, int64_t seq, i
   return launch_ab<128>((int)heads, (int)seq, block_row_ptr, block_col_idx, block_row_idx, pl, n_row_units,
                         n_col_units, n_aux, Q, K, V, O, dO, lse, dQ, dK, dV, (float)scale, w, st);
 }
+
+#ifdef TSB_TC_TRACE
+extern "C" __attribute__((visibility("default"))) int trnsparse_ab_trace_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, tsb::g_ab_trace, sizeof(tsb::g_ab_trace));
+}
+#endif
