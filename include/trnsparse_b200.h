@@ -423,6 +423,43 @@ TRNSPARSE_API int trnsparse_bsr_cg_noalloc(int64_t m, int64_t n, int b, int64_t 
                              int x_is_zero, const float* inv_d, double tol, int max_iter,
                              void* status_out, void* stream);
 
+/* ---- device-side format construction --------------------------------
+ * BSRMatrix.from_dense (trnsparse/formats.py:184-221): a block is kept iff
+ * max |v| over the block (zero-padded past the matrix edge) exceeds the
+ * threshold; kept blocks in row-major block order. Two calls: _count fills
+ * block_row_ptr (int64 [ceil(m/b) + 1], device) and keeps the block slots in
+ * ws; the caller reads block_row_ptr's last entry (the block count),
+ * allocates, and _fill writes blocks (n_blocks x b x b, A's dtype) and
+ * block_col_idx (int64). threshold: already rounded to A's dtype. A: row-major
+ * m x n with leading dimension lda (elements); dtype F32 or BF16. */
+TRNSPARSE_API size_t trnsparse_bsr_from_dense_workspace_size(int64_t m, int64_t n, int block_size);
+TRNSPARSE_API int trnsparse_bsr_from_dense_count(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                   int block_size, float threshold, long long* block_row_ptr, void* ws,
+                                   size_t ws_bytes, void* stream);
+TRNSPARSE_API int trnsparse_bsr_from_dense_fill(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                  int block_size, void* blocks, long long* block_col_idx, const void* ws,
+                                  void* stream);
+/* CSR from_dense (formats.py:269-278): entries with |v| > threshold, row by
+ * row in column order. _count fills row_ptr (int64 [m + 1]); _fill writes
+ * values (A's dtype) and col_idx (int64). */
+TRNSPARSE_API size_t trnsparse_csr_from_dense_workspace_size(int64_t m);
+TRNSPARSE_API int trnsparse_csr_from_dense_count(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                   float threshold, long long* row_ptr, void* ws, size_t ws_bytes,
+                                   void* stream);
+TRNSPARSE_API int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                  float threshold, const long long* row_ptr, void* values, long long* col_idx,
+                                  void* stream);
+/* COOMatrix.to_csr (formats.py:104-124): entries ordered by (row, col),
+ * entries with equal (row, col) in input order (a stable sort). rows, cols:
+ * int64 device arrays of nnz entries (nnz < 2^32, n < 2^31); values of dtype
+ * F32, F64, BF16 or F16. Outputs: row_ptr (int64 [m + 1]), cols_out (int64),
+ * values_out. Synchronises the stream once to report out-of-range indices
+ * (TRNSPARSE_ERR_ARG). */
+TRNSPARSE_API size_t trnsparse_coo_to_csr_workspace_size(int64_t m, int64_t nnz);
+TRNSPARSE_API int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const long long* rows,
+                         const long long* cols, const void* values, int dtype, long long* row_ptr,
+                         long long* cols_out, void* values_out, void* ws, size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,14 @@ SIGNATURES.update({
     "trnsparse_bsr_attention_tc_lse": [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _f64, _p],
     "trnsparse_bsr_attention_backward_tc_plan": [_i64, _i64, _p, _p, _i32, _p, _i64, _p],
     "trnsparse_bsr_attention_backward_tc_workspace_size": [_i64, _i64, _i64, _i64],
+    "trnsparse_bsr_from_dense_workspace_size": [_i64, _i64, _i32],
+    "trnsparse_bsr_from_dense_count": [_i64, _i64, _p, _i64, _i32, _i32, C.c_float, _p, _p, _sz, _p],
+    "trnsparse_bsr_from_dense_fill": [_i64, _i64, _p, _i64, _i32, _i32, _p, _p, _p, _p],
+    "trnsparse_csr_from_dense_workspace_size": [_i64],
+    "trnsparse_csr_from_dense_count": [_i64, _i64, _p, _i64, _i32, C.c_float, _p, _p, _sz, _p],
+    "trnsparse_csr_from_dense_fill": [_i64, _i64, _p, _i64, _i32, C.c_float, _p, _p, _p, _p],
+    "trnsparse_coo_to_csr_workspace_size": [_i64, _i64],
+    "trnsparse_coo_to_csr": [_i64, _i64, _i64, _p, _p, _p, _i32, _p, _p, _p, _p, _sz, _p],
     "trnsparse_bsr_attention_backward_tc": [_i64, _i64, _i64, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _p, _p,
                                             _p, _p, _p, _p, _p, _f64, _p, _sz, _p],
     "trnsparse_bsr_cg_layout": [_i64, _i32, C.POINTER(C.c_size_t)],
@@ -97,6 +105,9 @@ _RESTYPE = {
     "trnsparse_bsr_cgcg_workspace_size": C.c_size_t,
     "trnsparse_bsr_attention_backward_workspace_size": C.c_size_t,
     "trnsparse_bsr_attention_backward_tc_workspace_size": C.c_size_t,
+    "trnsparse_bsr_from_dense_workspace_size": C.c_size_t,
+    "trnsparse_csr_from_dense_workspace_size": C.c_size_t,
+    "trnsparse_coo_to_csr_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_plan_capacity": C.c_int64,
     "trnsparse_screened_spmm_workspace_size": C.c_size_t,
     "trnsparse_peer_comm_bytes": C.c_size_t,

@@ -8,6 +8,11 @@ time an op runs on a matrix, its index arrays and values are copied once to
 the GPU in the layout the kernels stream (int32 or int64 indices, contiguous
 ``(n_blocks, b, b)`` blocks), and the copy is reused until a field is
 replaced or modified in place.
+
+Construction from a dense CUDA tensor (``BSRMatrix.from_dense``,
+``from_dense``) and ``COOMatrix.to_csr`` of CUDA tensors run on the device
+(csrc/formats.cu) and give the same structure and values as the host path
+bit for bit; their results stay on the device.
 """
 
 from __future__ import annotations
@@ -16,6 +21,26 @@ from dataclasses import dataclass, field
 from typing import Any
 
 import torch
+
+
+def _threshold_in(dtype: torch.dtype, threshold: float) -> float:
+    """``threshold`` rounded to ``dtype``: torch compares a tensor with a
+    Python scalar in the tensor's dtype (``|v| > 0.1`` is false for the
+    float32 0.1)."""
+    return float(torch.tensor(float(threshold), dtype=torch.float64).to(dtype).to(torch.float64))
+
+
+def _dense_args(A: torch.Tensor):
+    """(A with unit column stride, its row stride, dtype code) for the C ABI."""
+    from . import _lib
+
+    if A.stride(-1) != 1 or (A.shape[0] > 1 and A.stride(0) < A.shape[1]):
+        A = A.contiguous()
+    lda = A.stride(0) if A.shape[0] > 1 else max(A.shape[1], 1)
+    return A, lda, _lib.dtype_code(A.dtype)
+
+
+_DEVICE_DENSE = (torch.float32, torch.bfloat16)
 
 
 def _ceil_to(v: int, b: int) -> int:
@@ -120,13 +145,18 @@ class COOMatrix:
 
     def to_dense(self) -> torch.Tensor:
         m, n = self.shape
-        dense = torch.zeros(m, n, dtype=self.dtype)
+        dense = torch.zeros(m, n, dtype=self.dtype, device=self.values.device)
         dense[self.row_indices, self.col_indices] = self.values
         return dense
 
     def to_csr(self) -> CSRMatrix:
-        """Sort entries by (row, col) and compress rows (formats.py:104-124)."""
+        """Sort entries by (row, col) and compress rows (formats.py:104-124).
+        Entries with equal (row, col) keep their order. CUDA tensors are
+        converted on the device."""
         m, n = self.shape
+        if self.values.is_cuda and self.values.dtype in (torch.float32, torch.float64, torch.bfloat16,
+                                                          torch.float16):
+            return self._to_csr_device()
         order = torch.argsort(self.row_indices * n + self.col_indices, stable=True)
         rows = self.row_indices[order]
         counts = torch.bincount(rows.to(torch.long).cpu(), minlength=m)[:m]
@@ -138,6 +168,26 @@ class COOMatrix:
             row_ptrs=row_ptrs,
             shape=self.shape,
         )
+
+    def _to_csr_device(self) -> CSRMatrix:
+        from . import _lib
+
+        m, n = self.shape
+        dev = self.values.device
+        rows = self.row_indices.to(device=dev, dtype=torch.int64).contiguous()
+        cols = self.col_indices.to(device=dev, dtype=torch.int64).contiguous()
+        vals = self.values.contiguous()
+        nnz = vals.shape[0]
+        row_ptrs = torch.empty(m + 1, dtype=torch.int64, device=dev)
+        cols_out = torch.empty(nnz, dtype=torch.int64, device=dev)
+        vals_out = torch.empty_like(vals)
+        ws_bytes = _lib.raw("trnsparse_coo_to_csr_workspace_size")(m, nnz)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("trnsparse_coo_to_csr", m, n, nnz, rows.data_ptr(), cols.data_ptr(), vals.data_ptr(),
+                      _lib.dtype_code(vals.dtype), row_ptrs.data_ptr(), cols_out.data_ptr(), vals_out.data_ptr(),
+                      ws.data_ptr(), ws_bytes, _lib.stream_handle(dev))
+        return CSRMatrix(values=vals_out, col_indices=cols_out, row_ptrs=row_ptrs, shape=self.shape)
 
     def __repr__(self) -> str:
         return f"COOMatrix(shape={self.shape}, nnz={self.nnz}, density={self.density:.4f})"
@@ -188,10 +238,13 @@ class BSRMatrix:
         """Keep block (i, j) iff some |A| entry in it exceeds ``threshold``.
 
         Blocks are ordered row-major over the block grid, so column indices
-        ascend within each block-row (formats.py:184-221).
+        ascend within each block-row (formats.py:184-221). A float32 or
+        bfloat16 CUDA tensor is screened and packed on the device.
         """
         b = block_size
         m, n = A.shape
+        if A.is_cuda and A.dtype in _DEVICE_DENSE:
+            return cls._from_dense_device(A, b, threshold)
         mp, np_ = _ceil_to(m, b), _ceil_to(n, b)
         if (mp, np_) != (m, n):
             Ap = A.new_zeros(mp, np_)
@@ -210,6 +263,30 @@ class BSRMatrix:
             shape=(m, n),
             block_size=b,
         )
+
+    @classmethod
+    def _from_dense_device(cls, A: torch.Tensor, b: int, threshold: float) -> BSRMatrix:
+        from . import _lib
+
+        m, n = A.shape
+        dev = A.device
+        A, lda, code = _dense_args(A)
+        mb, nbc = _ceil_to(m, b) // b, _ceil_to(n, b) // b
+        row_ptrs = torch.empty(mb + 1, dtype=torch.int64, device=dev)
+        ws_bytes = _lib.raw("trnsparse_bsr_from_dense_workspace_size")(m, n, b)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+        thr = _threshold_in(A.dtype, threshold)
+        with torch.cuda.device(dev):
+            st = _lib.stream_handle(dev)
+            _lib.call("trnsparse_bsr_from_dense_count", m, n, A.data_ptr(), lda, code, b, thr, row_ptrs.data_ptr(),
+                      ws.data_ptr(), ws_bytes, st)
+            nb = int(row_ptrs[-1].item()) if mb > 0 else 0
+            blocks = torch.empty(nb, b, b, dtype=A.dtype, device=dev)
+            cols = torch.empty(nb, dtype=torch.int64, device=dev)
+            if nb > 0:
+                _lib.call("trnsparse_bsr_from_dense_fill", m, n, A.data_ptr(), lda, code, b, blocks.data_ptr(),
+                          cols.data_ptr(), ws.data_ptr(), st)
+        return cls(blocks=blocks, block_col_indices=cols, block_row_ptrs=row_ptrs, shape=(m, n), block_size=b)
 
     @classmethod
     def from_csr(cls, csr: CSRMatrix, block_size: int = 128, threshold: float = 0.0) -> BSRMatrix:
@@ -263,12 +340,38 @@ class BSRMatrix:
 
 
 def from_dense(A: torch.Tensor, threshold: float = 0.0) -> CSRMatrix:
-    """Dense -> CSR keeping entries with |v| > threshold (formats.py:269-278)."""
+    """Dense -> CSR keeping entries with |v| > threshold (formats.py:269-278).
+    A float32 or bfloat16 CUDA tensor is converted on the device."""
     m, n = A.shape
+    if A.is_cuda and A.dtype in _DEVICE_DENSE:
+        return _csr_from_dense_device(A, threshold)
     keep = A.abs() > threshold
     rows, cols = torch.where(keep)
     coo = COOMatrix(values=A[keep], row_indices=rows, col_indices=cols, shape=(m, n))
     return coo.to_csr()
+
+
+def _csr_from_dense_device(A: torch.Tensor, threshold: float) -> CSRMatrix:
+    from . import _lib
+
+    m, n = A.shape
+    dev = A.device
+    A, lda, code = _dense_args(A)
+    thr = _threshold_in(A.dtype, threshold)
+    row_ptrs = torch.empty(m + 1, dtype=torch.int64, device=dev)
+    ws_bytes = _lib.raw("trnsparse_csr_from_dense_workspace_size")(m)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.stream_handle(dev)
+        _lib.call("trnsparse_csr_from_dense_count", m, n, A.data_ptr(), lda, code, thr, row_ptrs.data_ptr(),
+                  ws.data_ptr(), ws_bytes, st)
+        nnz = int(row_ptrs[-1].item())
+        vals = torch.empty(nnz, dtype=A.dtype, device=dev)
+        cols = torch.empty(nnz, dtype=torch.int64, device=dev)
+        if nnz > 0:
+            _lib.call("trnsparse_csr_from_dense_fill", m, n, A.data_ptr(), lda, code, thr, row_ptrs.data_ptr(),
+                      vals.data_ptr(), cols.data_ptr(), st)
+    return CSRMatrix(values=vals, col_indices=cols, row_ptrs=row_ptrs, shape=(m, n))
 
 
 def from_scipy(sp_matrix) -> CSRMatrix:
