@@ -458,6 +458,75 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
     nb = A5.n_blocks * 128 * 128 * 4 + 4 * A5.n_blocks + 4 * 2049 + 8 * A5.shape[0]
     ex["config5_bsr_spmv"] = {"GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
                               "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
+    del A5, M5, bd, xv
+    ex.update(run_format_extras(pk))
+    return ex
+
+
+def time_eager(f, reps: int) -> float:
+    """Median device milliseconds of ``f`` run eagerly (for calls that read a count back
+    to the host mid-way and so cannot be captured in a graph)."""
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        f()
+        b.record()
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(b))
+    out.sort()
+    return out[len(out) // 2]
+
+
+def run_format_extras(pk: dict) -> dict:
+    """Device-side format construction (csrc/formats.cu): algorithmic bytes = the dense
+    input read once + the sparse output written (COO: indices and values read, sorted
+    output written); inputs exceed L2."""
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+
+    ex = {}
+    g = torch.Generator().manual_seed(0)
+    n, b = 16384, 128
+    keep = torch.rand(n // b, n // b, generator=g) < 0.25
+    A = torch.randn(n, n, generator=g)
+    A.mul_(keep.repeat_interleave(b, 0).repeat_interleave(b, 1))
+    Ad = A.cuda()
+    del A
+    bsr = ts.BSRMatrix.from_dense(Ad, block_size=b)
+    ms = time_eager(lambda: ts.BSRMatrix.from_dense(Ad, block_size=b), 5)
+    nb = Ad.numel() * 4 + bsr.n_blocks * (b * b * 4 + 8) + 8 * (n // b + 1)
+    ex["formats_bsr_from_dense_16384_p025"] = {
+        "ms": round(ms, 3), "GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "n_blocks": bsr.n_blocks,
+        "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3),
+        "note": "screen pass reads A; fill pass re-reads the kept blocks (not counted); one host read of the count"}
+    del bsr
+    Ad = torch.randn(8192, 8192, generator=g).cuda()
+    Ad[torch.rand(8192, 8192, device="cuda") < 0.983] = 0.0
+    csr = ts.from_dense(Ad)
+    ms = time_eager(lambda: ts.from_dense(Ad), 5)
+    nb = Ad.numel() * 4 + csr.nnz * 12 + 8 * 8193
+    ex["formats_csr_from_dense_8192_d0017"] = {
+        "ms": round(ms, 3), "GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "nnz": csr.nnz,
+        "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3),
+        "note": "count and fill passes both read A (second read not counted)"}
+    del Ad, csr
+    A2 = w.poisson2d_csr(2048)
+    counts = (A2.row_ptrs[1:] - A2.row_ptrs[:-1]).long()
+    rows = torch.repeat_interleave(torch.arange(A2.shape[0]), counts)
+    perm = torch.randperm(rows.numel(), generator=g)
+    coo = ts.COOMatrix(values=A2.values[perm].cuda(), row_indices=rows[perm].cuda(),
+                       col_indices=A2.col_indices[perm].long().cuda(), shape=A2.shape)
+    ms = time_eager(lambda: coo.to_csr(), 5)
+    nnz = coo.nnz
+    nb = nnz * (8 + 8 + 4) + nnz * (8 + 4) + 8 * (A2.shape[0] + 1)
+    ex["formats_coo_to_csr_config2_shuffled"] = {
+        "ms": round(ms, 3), "GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "nnz": nnz,
+        "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3),
+        "note": "config-2 Poisson entries in random order; includes the index check read-back"}
     return ex
 
 

@@ -3,7 +3,7 @@
 // (formats.py:269-278) and COOMatrix.to_csr (formats.py:104-124), with the
 // same results bit for bit.
 //
-//   BSR from dense   a CTA per 128x128 (b x b) block screens max |v| (a NaN
+//   BSR from dense   a CTA per b x b block screens max |v| (a NaN
 //                    in the block drops it, as torch.amax propagates NaN) and
 //                    writes a 0/1 count; one exclusive scan over the block
 //                    grid in row-major order gives every kept block its slot
@@ -12,15 +12,18 @@
 //                    with zeros past the matrix edge.
 //   CSR from dense   a warp per row counts |v| > threshold, a scan gives the
 //                    row pointers, and a second pass compacts each row in
-//                    column order with warp ballots.
+//                    column order (per-lane counts, a warp prefix sum).
+// Dense rows are read in 16-byte pieces where the leading dimension and the
+// base allow it.
 //   COO -> CSR       row histogram (atomics) and scan, an atomic-cursor
 //                    scatter of (col << 32 | entry index) keys into their row,
 //                    then a sort of each row's keys: the entry index breaks
 //                    ties, so the result is the stable (row, col) order of
 //                    torch.argsort(rows * n + cols, stable=True). Rows of up to
-//                    32 entries sort in a warp (shuffle bitonic), longer rows in a
-//                    CTA (shared-memory bitonic over 2048-key chunks, then
-//                    merge passes through a second key buffer).
+//                    8 entries sort in one thread's registers, up to 32 in a warp
+//                    (shuffle bitonic), longer ones in a CTA (shared-memory
+//                    bitonic over 2048-key chunks, then merge passes through a
+//                    second key buffer); the thread-per-row pass lists the others.
 // Thresholds compare in the matrix's dtype: the caller passes the threshold
 // already rounded to it (torch rounds a Python scalar to the tensor's dtype).
 #include <cuda_bf16.h>
@@ -130,8 +133,50 @@ int exclusive_scan(long long* v, int64_t n, long long* part, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------- BSR from dense
+// VEC elements (16 bytes) per load when the rows allow it, else one
+template <typename T, int VEC> struct Vec;
+template <typename T> struct Vec<T, 1> {
+  T v[1];
+};
+template <> struct alignas(16) Vec<float, 4> {
+  float v[4];
+};
+template <> struct alignas(16) Vec<__nv_bfloat16, 8> {
+  __nv_bfloat16 v[8];
+};
+
+// Warp w of the CTA walks rows w, w + 8, ... of the block; lanes cover the row in VEC-wide
+// pieces. f(piece, k, valid) sees every element of the block that lies inside the matrix.
+template <typename T, int VEC, typename F>
+__device__ __forceinline__ void for_block_rows(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda, int b,
+                                               int64_t r0, int64_t c0, F&& f) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  for (int r = warp; r < b; r += warps) {
+    const int64_t gr = r0 + r;
+    if (gr >= m) break;
+    const T* row = A + gr * lda + c0;
+    for (int c = lane * VEC; c < b; c += 32 * VEC) {
+      if (c0 + c + VEC <= n) {
+        f(r, c, *reinterpret_cast<const Vec<T, VEC>*>(row + c), VEC);
+      } else {
+        Vec<T, VEC> x;
+        int cnt = 0;
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          x.v[k] = T(0.f);
+          if (c0 + c + k < n) {
+            x.v[k] = row[c + k];
+            cnt = k + 1;
+          }
+        }
+        f(r, c, x, cnt);
+      }
+    }
+  }
+}
+
 // grid (block column, block row); writes pos[1 + i * nbc + j] = keep ? 1 : 0
-template <typename T>
+template <typename T, int VEC>
 __global__ void __launch_bounds__(256) bsr_screen_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda,
                                                          int b, float thr, int64_t nbc, long long* __restrict__ pos) {
   __shared__ float smax[8];
@@ -139,15 +184,16 @@ __global__ void __launch_bounds__(256) bsr_screen_kernel(int64_t m, int64_t n, c
   const int64_t j = blockIdx.x, i = blockIdx.y;
   float mx = 0.f;
   int nan = 0;
-  const int64_t bb = static_cast<int64_t>(b) * b;
-  for (int64_t e = threadIdx.x; e < bb; e += blockDim.x) {
-    const int64_t r = i * b + e / b, c = j * b + e % b;
-    if (r < m && c < n) {
-      const float a = fm_abs<T>(A[r * lda + c]);
-      nan |= a != a;
-      mx = fmaxf(mx, a);
+  for_block_rows<T, VEC>(m, n, A, lda, b, i * b, j * b, [&](int, int, const Vec<T, VEC>& x, int cnt) {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      if (k < cnt) {
+        const float a = fm_abs<T>(x.v[k]);
+        nan |= a != a;
+        mx = fmaxf(mx, a);
+      }
     }
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -163,7 +209,7 @@ __global__ void __launch_bounds__(256) bsr_screen_kernel(int64_t m, int64_t n, c
       mx = fmaxf(mx, smax[w]);
       nan |= snan[w];
     }
-    // padding zeros take part in the max, as in the reference's padded grid
+    // padding zeros take part in the max (it starts at 0), as in the reference's padded grid
     pos[1 + i * nbc + j] = (!nan && mx > thr) ? 1 : 0;
   }
 }
@@ -175,8 +221,8 @@ __global__ void bsr_row_ptr_kernel(int64_t mb, int64_t nbc, const long long* __r
     row_ptr[i] = pos[i * nbc];
 }
 
-// grid (block column, block row): copy a kept block to its slot
-template <typename T>
+// grid (block column, block row): copy a kept block to its slot, zeros past the matrix edge
+template <typename T, int VEC>
 __global__ void __launch_bounds__(256) bsr_fill_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda,
                                                        int b, int64_t nbc, const long long* __restrict__ pos,
                                                        T* __restrict__ blocks, long long* __restrict__ col_idx) {
@@ -185,16 +231,46 @@ __global__ void __launch_bounds__(256) bsr_fill_kernel(int64_t m, int64_t n, con
   const long long slot = pos[k];
   if (pos[k + 1] == slot) return;  // dropped
   if (threadIdx.x == 0) col_idx[slot] = j;
-  const int64_t bb = static_cast<int64_t>(b) * b;
-  T* dst = blocks + slot * bb;
-  for (int64_t e = threadIdx.x; e < bb; e += blockDim.x) {
-    const int64_t r = i * b + e / b, c = j * b + e % b;
-    dst[e] = (r < m && c < n) ? A[r * lda + c] : T(0.f);
+  T* dst = blocks + slot * static_cast<int64_t>(b) * b;
+  const bool ragged = (i + 1) * b > m || (j + 1) * b > n;
+  if (ragged) {  // clear first: rows past the edge are skipped below
+    for (int e = threadIdx.x; e < b * b; e += blockDim.x) dst[e] = T(0.f);
+    __syncthreads();
   }
+  for_block_rows<T, VEC>(m, n, A, lda, b, i * b, j * b, [&](int r, int c, const Vec<T, VEC>& x, int cnt) {
+    if (cnt == VEC) {
+      *reinterpret_cast<Vec<T, VEC>*>(dst + r * b + c) = x;
+    } else {
+#pragma unroll
+      for (int q = 0; q < VEC; ++q)
+        if (q < cnt) dst[r * b + c + q] = x.v[q];
+    }
+  });
 }
 
 // ---------------------------------------------------------------- CSR from dense
-template <typename T>
+// a warp per row; lane l covers elements [j0 + VEC l, j0 + VEC l + VEC) of each 32 VEC piece
+template <typename T, int VEC>
+__device__ __forceinline__ Vec<T, VEC> load_piece(const T* row, int64_t j, int64_t n, int& cnt) {
+  Vec<T, VEC> x;
+  if (j + VEC <= n) {
+    x = *reinterpret_cast<const Vec<T, VEC>*>(row + j);
+    cnt = VEC;
+  } else {
+    cnt = 0;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      x.v[k] = T(0.f);
+      if (j + k < n) {
+        x.v[k] = row[j + k];
+        cnt = k + 1;
+      }
+    }
+  }
+  return x;
+}
+
+template <typename T, int VEC>
 __global__ void csr_count_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda, float thr,
                                  long long* __restrict__ v) {
   const int lane = threadIdx.x & 31;
@@ -202,14 +278,20 @@ __global__ void csr_count_kernel(int64_t m, int64_t n, const T* __restrict__ A, 
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
     const T* row = A + r * lda;
     long long c = 0;
-    for (int64_t j = lane; j < n; j += 32) c += fm_abs<T>(row[j]) > thr ? 1 : 0;
+#pragma unroll 4
+    for (int64_t j = lane * VEC; j < n; j += 32 * VEC) {
+      int cnt;
+      const Vec<T, VEC> x = load_piece<T, VEC>(row, j, n, cnt);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) c += (k < cnt && fm_abs<T>(x.v[k]) > thr) ? 1 : 0;
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
     if (lane == 0) v[1 + r] = c;
   }
 }
 
-template <typename T>
+template <typename T, int VEC>
 __global__ void csr_fill_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda, float thr,
                                 const long long* __restrict__ row_ptr, T* __restrict__ vals,
                                 long long* __restrict__ cols) {
@@ -218,21 +300,34 @@ __global__ void csr_fill_kernel(int64_t m, int64_t n, const T* __restrict__ A, i
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
     const T* row = A + r * lda;
     long long o = row_ptr[r];
-    for (int64_t j0 = 0; j0 < n; j0 += 32) {
-      const int64_t j = j0 + lane;
-      T x = T(0.f);
-      bool keep = false;
-      if (j < n) {
-        x = row[j];
-        keep = fm_abs<T>(x) > thr;
+    for (int64_t j0 = 0; j0 < n; j0 += 32 * VEC) {
+      const int64_t j = j0 + lane * VEC;
+      int cnt = 0;
+      Vec<T, VEC> x;
+      if (j < n) x = load_piece<T, VEC>(row, j, n, cnt);
+      unsigned keep = 0;
+#pragma unroll
+      for (int k = 0; k < VEC; ++k)
+        if (k < cnt && fm_abs<T>(x.v[k]) > thr) keep |= 1u << k;
+      if (!__any_sync(0xffffffffu, keep != 0)) continue;  // nothing kept in this piece of the row
+      // exclusive prefix of the kept counts over the lanes: entries stay in column order
+      const int mine = __popc(keep);
+      int inc = mine;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += y;
       }
-      const unsigned ball = __ballot_sync(0xffffffffu, keep);
-      if (keep) {
-        const long long p = o + __popc(ball & ((1u << lane) - 1u));
-        vals[p] = x;
-        cols[p] = j;
+      long long p = o + inc - mine;
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        if (keep & (1u << k)) {
+          vals[p] = x.v[k];
+          cols[p] = j + k;
+          ++p;
+        }
       }
-      o += __popc(ball);
+      o += __shfl_sync(0xffffffffu, inc, 31);
     }
   }
 }
@@ -255,12 +350,28 @@ __global__ void coo_count_kernel(int64_t nnz, int64_t m, int64_t n, const long l
 __global__ void coo_scatter_kernel(int64_t nnz, int64_t m, int64_t n, const long long* __restrict__ rows,
                                    const long long* __restrict__ cols, unsigned long long* __restrict__ cursor,
                                    unsigned long long* __restrict__ keys) {
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < nnz;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const long long r = rows[e], c = cols[e];
-    if (r < 0 || r >= m || c < 0 || c >= n) continue;
-    const unsigned long long p = atomicAdd(cursor + r, 1ull);
-    keys[p] = (static_cast<unsigned long long>(c) << 32) | static_cast<unsigned long long>(e);
+  // four entries per thread and sweep: four cursor atomics in flight at once
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t e0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e0 < nnz; e0 += 4 * stride) {
+    long long r[4], c[4];
+    unsigned long long p[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t e = e0 + u * stride;
+      r[u] = -1;
+      if (e < nnz) {
+        r[u] = rows[e];
+        c[u] = cols[e];
+        if (r[u] >= m || c[u] < 0 || c[u] >= n) r[u] = -1;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (r[u] >= 0) p[u] = atomicAdd(cursor + r[u], 1ull);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (r[u] >= 0)
+        keys[p[u]] = (static_cast<unsigned long long>(c[u]) << 32) | static_cast<unsigned long long>(e0 + u * stride);
   }
 }
 
@@ -277,25 +388,65 @@ __device__ __forceinline__ void coo_emit(unsigned long long key, long long p, co
     reinterpret_cast<uint64_t*>(vals_out)[p] = reinterpret_cast<const uint64_t*>(vals_in)[src];
 }
 
-// rows of at most 32 entries: a warp each, bitonic sort through shuffles
-__global__ void coo_sort_short_kernel(int64_t m, const long long* __restrict__ row_ptr,
-                                      const unsigned long long* __restrict__ keys, const uint8_t* __restrict__ vals_in,
-                                      int esz, long long* __restrict__ cols_out, uint8_t* __restrict__ vals_out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+constexpr int kTiny = 8;  // rows of up to kTiny entries sort in one thread's registers
+
+// A thread per row: rows of at most kTiny entries are sorted in registers (an unrolled
+// exchange network); longer rows are listed for the warp (<= 32) or CTA passes.
+__global__ void coo_sort_tiny_kernel(int64_t m, const long long* __restrict__ row_ptr,
+                                     const unsigned long long* __restrict__ keys, const uint8_t* __restrict__ vals_in,
+                                     int esz, long long* __restrict__ cols_out, uint8_t* __restrict__ vals_out,
+                                     long long* __restrict__ mid_rows, unsigned long long* __restrict__ n_mid,
+                                     long long* __restrict__ long_rows, unsigned long long* __restrict__ n_long) {
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < m;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const long long b0 = row_ptr[r], len = row_ptr[r + 1] - b0;
-    if (len == 0 || len > 32) continue;
+    if (len > 32) {
+      long_rows[atomicAdd(n_long, 1ull)] = r;
+      continue;
+    }
+    if (len > kTiny) {
+      mid_rows[atomicAdd(n_mid, 1ull)] = r;
+      continue;
+    }
+    unsigned long long k[kTiny];
+#pragma unroll
+    for (int i = 0; i < kTiny; ++i) k[i] = i < len ? keys[b0 + i] : ~0ull;
+#pragma unroll
+    for (int i = 0; i < kTiny - 1; ++i) {
+#pragma unroll
+      for (int j = 0; j < kTiny - 1 - i; ++j) {
+        const unsigned long long a = k[j], c = k[j + 1];
+        k[j] = a < c ? a : c;
+        k[j + 1] = a < c ? c : a;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kTiny; ++i)
+      if (i < len) coo_emit(k[i], b0 + i, vals_in, esz, cols_out, vals_out);
+  }
+}
+
+// A warp per listed row of kTiny < len <= 32 entries: bitonic sort through shuffles.
+__global__ void coo_sort_mid_kernel(const long long* __restrict__ row_ptr, const long long* __restrict__ mid_rows,
+                                    const unsigned long long* __restrict__ n_mid,
+                                    const unsigned long long* __restrict__ keys, const uint8_t* __restrict__ vals_in,
+                                    int esz, long long* __restrict__ cols_out, uint8_t* __restrict__ vals_out) {
+  const int lane = threadIdx.x & 31;
+  const long long n_rows = static_cast<long long>(*n_mid);
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long q = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); q < n_rows;
+       q += warps) {
+    const long long r = mid_rows[q];
+    const long long b0 = row_ptr[r], len = row_ptr[r + 1] - b0;
     unsigned long long k = lane < len ? keys[b0 + lane] : ~0ull;
 #pragma unroll
     for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
       for (int stride = size >> 1; stride > 0; stride >>= 1) {
         const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, stride);
-        const bool up = (lane & size) == 0;          // ascending half of this bitonic stage
-        const bool lower = (lane & stride) == 0;     // this lane keeps the smaller key when ascending
-        const bool take_min = (up == lower);
-        k = take_min ? (o < k ? o : k) : (o > k ? o : k);
+        const bool up = (lane & size) == 0;        // ascending half of this bitonic stage
+        const bool lower = (lane & stride) == 0;   // this lane keeps the smaller key when ascending
+        k = (up == lower) ? (o < k ? o : k) : (o > k ? o : k);
       }
     }
     if (lane < len) coo_emit(k, b0 + lane, vals_in, esz, cols_out, vals_out);
@@ -336,15 +487,17 @@ __device__ __forceinline__ long long lower_bound_u64(const unsigned long long* p
   return lo;
 }
 
-// rows of more than 32 entries: a CTA each (grid-stride over the rows)
+// rows of more than 32 entries (listed by the tiny pass): a CTA each
 __global__ void __launch_bounds__(kSortThreads) coo_sort_long_kernel(
-    int64_t m, const long long* __restrict__ row_ptr, unsigned long long* __restrict__ keys,
+    const long long* __restrict__ row_ptr, const long long* __restrict__ long_rows,
+    const unsigned long long* __restrict__ n_long, unsigned long long* __restrict__ keys,
     unsigned long long* __restrict__ keys2, const uint8_t* __restrict__ vals_in, int esz,
     long long* __restrict__ cols_out, uint8_t* __restrict__ vals_out) {
   __shared__ unsigned long long s[kSortChunk];
-  for (int64_t r = blockIdx.x; r < m; r += gridDim.x) {
+  const long long n_rows = static_cast<long long>(*n_long);
+  for (long long q = blockIdx.x; q < n_rows; q += gridDim.x) {
+    const long long r = long_rows[q];
     const long long b0 = row_ptr[r], len = row_ptr[r + 1] - b0;
-    if (len <= 32) continue;
     unsigned long long* src = keys + b0;
     unsigned long long* dst = keys2 + b0;
     // sort each chunk in shared memory
@@ -394,6 +547,11 @@ unsigned grid_for(int64_t items, int per_cta) {
   return (unsigned)(g < 1 ? 1 : g);
 }
 
+// Launch a kernel templated on <T, VEC> with 16-byte pieces when rows and bases allow.
+bool vec_ok(const void* p, int64_t lda, int64_t b, int vec) {
+  return aligned16(p) && lda % vec == 0 && b % vec == 0;
+}
+
 }  // namespace
 }  // namespace tsb
 
@@ -421,11 +579,18 @@ extern "C" int trnsparse_bsr_from_dense_count(int64_t m, int64_t n, const void* 
   long long* part = pos + mb * nbc + 1;
   if (mb * nbc > 0) {
     dim3 g((unsigned)nbc, (unsigned)mb);
-    if (dtype == TRNSPARSE_F32)
-      bsr_screen_kernel<float><<<g, 256, 0, st>>>(m, n, (const float*)A, lda, block_size, threshold, nbc, pos);
-    else
-      bsr_screen_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(m, n, (const __nv_bfloat16*)A, lda, block_size, threshold,
-                                                          nbc, pos);
+    if (dtype == TRNSPARSE_F32) {
+      if (vec_ok(A, lda, block_size, 4))
+        bsr_screen_kernel<float, 4><<<g, 256, 0, st>>>(m, n, (const float*)A, lda, block_size, threshold, nbc, pos);
+      else
+        bsr_screen_kernel<float, 1><<<g, 256, 0, st>>>(m, n, (const float*)A, lda, block_size, threshold, nbc, pos);
+    } else {
+      using B16 = __nv_bfloat16;
+      if (vec_ok(A, lda, block_size, 8))
+        bsr_screen_kernel<B16, 8><<<g, 256, 0, st>>>(m, n, (const B16*)A, lda, block_size, threshold, nbc, pos);
+      else
+        bsr_screen_kernel<B16, 1><<<g, 256, 0, st>>>(m, n, (const B16*)A, lda, block_size, threshold, nbc, pos);
+    }
     TSB_CHECK_LAUNCH("bsr_from_dense: screen");
   }
   int rc = exclusive_scan(pos, mb * nbc, part, st);
@@ -447,12 +612,22 @@ extern "C" int trnsparse_bsr_from_dense_fill(int64_t m, int64_t n, const void* A
   cudaStream_t st = as_stream(stream);
   const long long* pos = static_cast<const long long*>(ws);
   dim3 g((unsigned)nbc, (unsigned)mb);
-  if (dtype == TRNSPARSE_F32)
-    bsr_fill_kernel<float><<<g, 256, 0, st>>>(m, n, (const float*)A, lda, block_size, nbc, pos, (float*)blocks,
-                                              block_col_idx);
-  else
-    bsr_fill_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(m, n, (const __nv_bfloat16*)A, lda, block_size, nbc, pos,
-                                                      (__nv_bfloat16*)blocks, block_col_idx);
+  if (dtype == TRNSPARSE_F32) {
+    if (vec_ok(A, lda, block_size, 4) && aligned16(blocks))
+      bsr_fill_kernel<float, 4><<<g, 256, 0, st>>>(m, n, (const float*)A, lda, block_size, nbc, pos, (float*)blocks,
+                                                   block_col_idx);
+    else
+      bsr_fill_kernel<float, 1><<<g, 256, 0, st>>>(m, n, (const float*)A, lda, block_size, nbc, pos, (float*)blocks,
+                                                   block_col_idx);
+  } else {
+    using B16 = __nv_bfloat16;
+    if (vec_ok(A, lda, block_size, 8) && aligned16(blocks))
+      bsr_fill_kernel<B16, 8><<<g, 256, 0, st>>>(m, n, (const B16*)A, lda, block_size, nbc, pos, (B16*)blocks,
+                                                 block_col_idx);
+    else
+      bsr_fill_kernel<B16, 1><<<g, 256, 0, st>>>(m, n, (const B16*)A, lda, block_size, nbc, pos, (B16*)blocks,
+                                                 block_col_idx);
+  }
   TSB_CHECK_LAUNCH("bsr_from_dense: fill");
   return TRNSPARSE_OK;
 }
@@ -475,11 +650,19 @@ extern "C" int trnsparse_csr_from_dense_count(int64_t m, int64_t n, const void* 
       cudaError_t e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
       return cuda_status(e, "csr_from_dense: empty rows");
     }
-    if (dtype == TRNSPARSE_F32)
-      csr_count_kernel<float><<<grid_for(m, 8), 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr);
-    else
-      csr_count_kernel<__nv_bfloat16><<<grid_for(m, 8), 256, 0, st>>>(m, n, (const __nv_bfloat16*)A, lda, threshold,
-                                                                    row_ptr);
+    const unsigned gr = grid_for(m, 8);
+    if (dtype == TRNSPARSE_F32) {
+      if (vec_ok(A, lda, 4, 4))
+        csr_count_kernel<float, 4><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr);
+      else
+        csr_count_kernel<float, 1><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr);
+    } else {
+      using B16 = __nv_bfloat16;
+      if (vec_ok(A, lda, 8, 8))
+        csr_count_kernel<B16, 8><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr);
+      else
+        csr_count_kernel<B16, 1><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr);
+    }
     TSB_CHECK_LAUNCH("csr_from_dense: count");
   }
   return exclusive_scan(row_ptr, m, static_cast<long long*>(ws), st);
@@ -493,12 +676,21 @@ extern "C" int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A
   if (m == 0 || n == 0) return TRNSPARSE_OK;
   TSB_REQUIRE(A && row_ptr && values && col_idx, "csr_from_dense: null pointer");
   cudaStream_t st = as_stream(stream);
-  if (dtype == TRNSPARSE_F32)
-    csr_fill_kernel<float><<<grid_for(m, 8), 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr,
-                                                          (float*)values, col_idx);
-  else
-    csr_fill_kernel<__nv_bfloat16><<<grid_for(m, 8), 256, 0, st>>>(m, n, (const __nv_bfloat16*)A, lda, threshold,
-                                                                  row_ptr, (__nv_bfloat16*)values, col_idx);
+  const unsigned gr = grid_for(m, 8);
+  if (dtype == TRNSPARSE_F32) {
+    if (vec_ok(A, lda, 4, 4))
+      csr_fill_kernel<float, 4><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr, (float*)values,
+                                                    col_idx);
+    else
+      csr_fill_kernel<float, 1><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr, (float*)values,
+                                                    col_idx);
+  } else {
+    using B16 = __nv_bfloat16;
+    if (vec_ok(A, lda, 8, 8))
+      csr_fill_kernel<B16, 8><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr, (B16*)values, col_idx);
+    else
+      csr_fill_kernel<B16, 1><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr, (B16*)values, col_idx);
+  }
   TSB_CHECK_LAUNCH("csr_from_dense: fill");
   return TRNSPARSE_OK;
 }
@@ -506,7 +698,7 @@ extern "C" int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A
 // ---------------------------------------------------------------- COO -> CSR
 extern "C" size_t trnsparse_coo_to_csr_workspace_size(int64_t m, int64_t nnz) {
   if (m < 0 || nnz < 0) return 0;
-  return sizeof(unsigned long long) * (size_t)(2 * nnz + m + 1) + scan_ws_bytes(m) + 16;
+  return sizeof(unsigned long long) * (size_t)(2 * nnz + 3 * m + 1) + scan_ws_bytes(m) + 32;
 }
 
 extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const long long* rows, const long long* cols,
@@ -524,9 +716,13 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
   unsigned long long* keys2 = keys + nnz;
   unsigned long long* cursor = keys2 + nnz;  // m entries
   long long* part = reinterpret_cast<long long*>(cursor + m + 1);
-  int* bad = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(part) + scan_ws_bytes(m));
+  long long* mid_rows = reinterpret_cast<long long*>(reinterpret_cast<uint8_t*>(part) + scan_ws_bytes(m));
+  long long* long_rows = mid_rows + m;
+  unsigned long long* n_mid = reinterpret_cast<unsigned long long*>(long_rows + m);
+  unsigned long long* n_long = n_mid + 1;
+  int* bad = reinterpret_cast<int*>(n_long + 1);
   cudaError_t e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(bad, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(n_mid, 0, 24, st);  // n_mid, n_long and bad
   if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
   if (nnz > 0) {
     coo_count_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols,
@@ -539,10 +735,13 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
   e = cudaMemcpyAsync(cursor, row_ptr, sizeof(long long) * m, cudaMemcpyDeviceToDevice, st);
   if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: cursors");
   coo_scatter_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols, cursor, keys);
-  coo_sort_short_kernel<<<grid_for(m, 8), 256, 0, st>>>(m, row_ptr, keys, (const uint8_t*)values, esz, cols_out,
-                                                       (uint8_t*)values_out);
-  coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(m, row_ptr, keys, keys2, (const uint8_t*)values, esz,
-                                                               cols_out, (uint8_t*)values_out);
+  coo_sort_tiny_kernel<<<grid_for(m, 256), 256, 0, st>>>(m, row_ptr, keys, (const uint8_t*)values, esz, cols_out,
+                                                        (uint8_t*)values_out, mid_rows, n_mid, long_rows, n_long);
+  coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, (const uint8_t*)values, esz,
+                                                     cols_out, (uint8_t*)values_out);
+  coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(row_ptr, long_rows, n_long, keys, keys2,
+                                                               (const uint8_t*)values, esz, cols_out,
+                                                               (uint8_t*)values_out);
   TSB_CHECK_LAUNCH("coo_to_csr: sort");
   // an out-of-range index is an argument error the caller sees on the host
   int hbad = 0;
