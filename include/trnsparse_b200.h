@@ -62,6 +62,19 @@ TRNSPARSE_API int trnsparse_csr_spmv(int64_t m, int64_t n, int64_t nnz, int inde
                        const void* row_ptrs, const void* col_indices, const void* values,
                        const void* x, double alpha, const void* y, double beta, void* out,
                        void* stream);
+/* spmv with x and y in pinned HOST memory (the reference's CPU-tensor call,
+ * ops.py:30-48, y = alpha A x): x is copied up in prefix pieces on a library
+ * copy stream, row chunk i ([row_splits[i], row_splits[i+1]), multiples of 4
+ * rows keep the vector path) runs once the first x_need[i] entries of x (the
+ * chunk's largest column + 1, non-decreasing) have arrived, and its rows are
+ * copied back on a second copy stream while later chunks compute. x_dev (n)
+ * and out_dev (m) are device scratch. `stream` waits for the last copy: after
+ * synchronising it, out_host is complete. row_splits / x_need: host arrays,
+ * n_chunks <= 64. Calls on one device are issued one at a time (a lock). */
+TRNSPARSE_API int trnsparse_csr_spmv_host(int64_t m, int64_t n, int64_t nnz, int index_type, int dtype,
+                            const void* row_ptrs, const void* col_indices, const void* values,
+                            const void* x_host, double alpha, void* out_host, void* x_dev, void* out_dev,
+                            int n_chunks, const int64_t* row_splits, const int64_t* x_need, void* stream);
 
 /* OUT = alpha * (A @ B) [+ beta * C]   (B is n x k, row stride ldb; C and OUT
  * are m x k with row stride ldc / ldo). Replaces nki_spmm

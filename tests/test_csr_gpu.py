@@ -141,3 +141,33 @@ def test_config2_full_size_poisson():
     ref = oracle.csr_spmm(A.row_ptrs, A.col_indices, A.values, A.shape, B)
     got = ts.spmm(A, B.cuda())
     assert rel_fro(got, ref) <= 1e-6
+
+
+@pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])
+def test_spmv_pinned_host_pipeline(index_dtype):
+    """A pinned host x on a large matrix takes the chunked pipeline (x up, row
+    chunks computed as their columns arrive, rows back on a second stream):
+    same values as the device-resident call, including a band matrix whose
+    row chunks reach far-away columns and a row chunk with no entries."""
+    from trnsparse_b200 import ops
+    from trnsparse_b200 import workloads as w
+
+    A = w.poisson2d_csr(1024, index_dtype=index_dtype)  # 1,048,576 rows
+    x = w.poisson_rhs(A.shape[0])
+    ref = ts.spmv(A, x.cuda(), alpha=2.0).cpu()
+    got = ts.spmv(A, x.pin_memory(), alpha=2.0)
+    assert not got.is_cuda and ops._SPMV_PIPE_MIN_ROWS <= A.shape[0]
+    torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
+    # first and last columns in every row, an empty middle: every chunk waits for all of x
+    n = 1 << 19
+    rp = torch.zeros(n + 1, dtype=torch.int64)
+    keep = torch.ones(n, dtype=torch.bool)
+    keep[n // 3: n // 3 + 100000] = False
+    counts = keep.long() * 2
+    rp[1:] = torch.cumsum(counts, 0)
+    ci = torch.stack([torch.zeros(n, dtype=torch.long), torch.full((n,), n - 1)], 1)[keep].reshape(-1)
+    vals = torch.randn(ci.numel(), generator=torch.Generator().manual_seed(8))
+    B = ts.CSRMatrix(values=vals, col_indices=ci.to(index_dtype), row_ptrs=rp.to(index_dtype), shape=(n, n))
+    xb = torch.randn(n, generator=torch.Generator().manual_seed(9))
+    torch.testing.assert_close(ts.spmv(B, xb.pin_memory()), ts.spmv(B, xb.cuda()).cpu(), rtol=1e-6, atol=1e-6)
+    assert ts._lib.device_error() == 0

@@ -30,6 +30,7 @@ SIGNATURES: dict[str, list] = {
     "trnsparse_last_error": [],
     "trnsparse_version": [],
     "trnsparse_csr_spmv": [_i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _f64, _p, _f64, _p, _p],
+    "trnsparse_csr_spmv_host": [_i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _f64, _p, _p, _p, _i32, _p, _p, _p],
     "trnsparse_csr_spmm": [_i64, _i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _i64, _f64, _p, _i64, _f64, _p, _i64, _p],
 }
 _BSR = [_i64, _i64, _i32, _i64, _p, _p, _p]  # m, n, b, n_blocks, row_ptr, col_idx, blocks

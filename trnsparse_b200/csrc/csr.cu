@@ -18,6 +18,8 @@
 
 #include <stdlib.h>
 
+#include <mutex>
+
 namespace tsb {
 namespace {
 
@@ -664,6 +666,118 @@ extern "C" int trnsparse_csr_spmv(int64_t m, int64_t n, int64_t nnz, int index_t
     return fail(TRNSPARSE_ERR_DTYPE, "csr_spmv: dtype %d not supported (F32, F64)", dtype);
   }
   return fail(TRNSPARSE_ERR_DTYPE, "csr_spmv: index type %d not supported (I32, I64)", index_type);
+}
+
+namespace {
+// Per-device copy streams and events of the host-buffer SpMV pipeline (created on first use).
+constexpr int kPipeMax = 64;
+struct PipeCtx {
+  bool ready = false;
+  cudaStream_t s_in = nullptr, s_out = nullptr;
+  cudaEvent_t start = nullptr, end = nullptr, in[kPipeMax] = {}, done[kPipeMax] = {};
+};
+PipeCtx g_pipe[64];
+std::mutex g_pipe_mu;
+
+int pipe_ctx(PipeCtx** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "csr_spmv_host: device");
+  if (dev < 0 || dev >= 64) return fail(TRNSPARSE_ERR_UNSUPPORTED, "csr_spmv_host: device %d", dev);
+  PipeCtx& c = g_pipe[dev];  // the caller holds g_pipe_mu
+  if (!c.ready) {
+    e = cudaStreamCreateWithFlags(&c.s_in, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c.s_out, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c.start, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c.end, cudaEventDisableTiming);
+    for (int i = 0; i < kPipeMax && e == cudaSuccess; ++i) {
+      e = cudaEventCreateWithFlags(&c.in[i], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c.done[i], cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "csr_spmv_host: streams");
+    c.ready = true;
+  }
+  *out = &c;
+  return TRNSPARSE_OK;
+}
+}  // namespace
+
+// y = alpha A x with x and y in pinned host memory: x goes up in prefix pieces on one copy
+// stream, row chunk i runs once the first x_need[i] entries of x have arrived, and its rows
+// go back on a second copy stream while later chunks compute; the caller's stream waits
+// for the last copy, so synchronising it (or any later work on it) sees y complete.
+extern "C" int trnsparse_csr_spmv_host(int64_t m, int64_t n, int64_t nnz, int index_type, int dtype,
+                                       const void* row_ptrs, const void* col_indices, const void* values,
+                                       const void* x_host, double alpha, void* out_host, void* x_dev, void* out_dev,
+                                       int n_chunks, const int64_t* row_splits, const int64_t* x_need,
+                                       void* stream) {
+  TSB_REQUIRE(m >= 0 && n >= 0 && nnz >= 0, "csr_spmv_host: negative size");
+  if (m == 0) return TRNSPARSE_OK;
+  TSB_REQUIRE(n_chunks > 0 && n_chunks <= kPipeMax, "csr_spmv_host: n_chunks must be 1..%d", kPipeMax);
+  TSB_REQUIRE(row_ptrs && x_host && out_host && x_dev && out_dev && row_splits && x_need,
+              "csr_spmv_host: null pointer");
+  TSB_REQUIRE(dtype == TRNSPARSE_F32 || dtype == TRNSPARSE_F64, "csr_spmv_host: dtype %d (F32, F64)", dtype);
+  TSB_REQUIRE(index_type == TRNSPARSE_I32 || index_type == TRNSPARSE_I64, "csr_spmv_host: index type %d",
+              index_type);
+  TSB_REQUIRE(row_splits[0] == 0 && row_splits[n_chunks] == m, "csr_spmv_host: row_splits must span [0, m)");
+  for (int i = 0; i < n_chunks; ++i)
+    TSB_REQUIRE(row_splits[i + 1] >= row_splits[i] && x_need[i] >= 0 && x_need[i] <= n &&
+                    (i == 0 || x_need[i] >= x_need[i - 1]),
+                "csr_spmv_host: row_splits ascending, x_need ascending within [0, n]");
+  std::lock_guard<std::mutex> lk(g_pipe_mu);  // one issue sequence at a time: the events are shared
+  PipeCtx* c = nullptr;
+  int rc = pipe_ctx(&c);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  const size_t es = dtype == TRNSPARSE_F32 ? 4 : 8, is = index_type == TRNSPARSE_I32 ? 4 : 8;
+  cudaError_t e = cudaEventRecord(c->start, st);  // the scratch buffers' earlier users come first
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_in, c->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->start, 0);
+  // x pieces: one per distinct prefix length
+  int64_t have = 0;
+  int piece[kPipeMax];
+  int np = 0;
+  for (int i = 0; i < n_chunks && e == cudaSuccess; ++i) {
+    if (x_need[i] > have) {
+      e = cudaMemcpyAsync(static_cast<uint8_t*>(x_dev) + have * es, static_cast<const uint8_t*>(x_host) + have * es,
+                          (x_need[i] - have) * es, cudaMemcpyHostToDevice, c->s_in);
+      if (e == cudaSuccess) e = cudaEventRecord(c->in[np], c->s_in);
+      have = x_need[i];
+      ++np;
+    }
+    piece[i] = np - 1;
+  }
+  int waited = -1;
+  for (int i = 0; i < n_chunks && e == cudaSuccess; ++i) {
+    const int64_t a = row_splits[i], b = row_splits[i + 1];
+    if (piece[i] > waited) {
+      e = cudaStreamWaitEvent(st, c->in[piece[i]], 0);
+      waited = piece[i];
+      if (e != cudaSuccess) break;
+    }
+    if (b > a) {
+      const void* rp = static_cast<const uint8_t*>(row_ptrs) + a * is;
+      void* o = static_cast<uint8_t*>(out_dev) + a * es;
+      if (dtype == TRNSPARSE_F32)
+        rc = index_type == TRNSPARSE_I32
+                 ? launch_spmv<int32_t, float>(b - a, nnz, rp, col_indices, values, x_dev, alpha, nullptr, 0.0, o, st)
+                 : launch_spmv<int64_t, float>(b - a, nnz, rp, col_indices, values, x_dev, alpha, nullptr, 0.0, o, st);
+      else
+        rc = index_type == TRNSPARSE_I32
+                 ? launch_spmv<int32_t, double>(b - a, nnz, rp, col_indices, values, x_dev, alpha, nullptr, 0.0, o, st)
+                 : launch_spmv<int64_t, double>(b - a, nnz, rp, col_indices, values, x_dev, alpha, nullptr, 0.0, o,
+                                                st);
+      if (rc) return rc;
+      e = cudaEventRecord(c->done[i], st);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->done[i], 0);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + a * es, o, (b - a) * es, cudaMemcpyDeviceToHost,
+                            c->s_out);
+    }
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(c->end, c->s_out);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, c->end, 0);
+  return cuda_status(e, "csr_spmv_host");
 }
 
 extern "C" int trnsparse_csr_spmm(int64_t m, int64_t n, int64_t k, int64_t nnz, int index_type, int dtype,

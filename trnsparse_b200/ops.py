@@ -74,12 +74,57 @@ def spmv(
     return _spmv_impl(A, x, alpha, y, beta)
 
 
+_SPMV_PIPE_CHUNKS = 4          # row / x chunks of the host-buffer pipeline (4 measured best of 4-32)
+_SPMV_PIPE_MIN_ROWS = 1 << 18  # smaller products are not worth splitting
+
+
+def _spmv_pipelined(A: CSRMatrix, lay: dict, x: torch.Tensor, alpha: float, dev: torch.device) -> torch.Tensor:
+    """``alpha * A @ x`` for a pinned host ``x`` through ``trnsparse_csr_spmv_host``:
+    x goes up in pieces, each row chunk's product starts once the x entries
+    its columns reach have arrived, and its rows come back while later chunks
+    still compute, so both PCIe directions and the kernel overlap."""
+    m, n = A.shape
+    K = _SPMV_PIPE_CHUNKS
+    key = ("spmv_pipe", K)
+    plan = lay.get(key)
+    if plan is None:
+        rp = lay["row_ptrs"].long()
+        ci = lay["col_indices"]
+        rstep = (-(-m // K) + 63) // 64 * 64  # ceil(m / K) rounded up to 64 rows
+        splits = list(range(0, m, rstep)) + [m]
+        bounds = rp[torch.tensor(splits, device=rp.device)].tolist()
+        need, top = [], 0
+        for i in range(len(splits) - 1):
+            lo, hi = bounds[i], bounds[i + 1]
+            if hi > lo:
+                top = max(top, int(ci[lo:hi].max().item()) + 1)
+            need.append(top)
+        plan = (len(splits) - 1, torch.tensor(splits, dtype=torch.int64), torch.tensor(need, dtype=torch.int64))
+        lay[key] = plan
+    nch, splits, need = plan
+    xd = torch.empty(n, dtype=A.dtype, device=dev)
+    out = torch.empty(m, dtype=A.dtype, device=dev)
+    host = torch.empty(m, dtype=A.dtype, pin_memory=True)
+    st = torch.cuda.current_stream(dev)
+    _lib.call("trnsparse_csr_spmv_host", m, n, A.nnz, _lib.index_code(lay["row_ptrs"].dtype), _lib.dtype_code(A.dtype),
+              _lib.ptr(lay["row_ptrs"]), _lib.ptr(lay["col_indices"]), _lib.ptr(lay["values"]), x.data_ptr(),
+              float(alpha), host.data_ptr(), xd.data_ptr(), out.data_ptr(), nch, splits.data_ptr(), need.data_ptr(),
+              st.cuda_stream)
+    st.synchronize()
+    return host
+
+
 def _spmv_impl(A: CSRMatrix, x: torch.Tensor, alpha: float, y, beta: float) -> torch.Tensor:
     m, n = A.shape
     dev = _dev_of(x)
     if x.dtype != A.dtype:
         raise RuntimeError(f"spmv: dtype mismatch, A is {A.dtype} and x is {x.dtype}")
     lay = A.device_layout(dev)
+    if (not x.is_cuda and x.is_pinned() and x.is_contiguous() and (y is None or beta == 0.0)
+            and m >= _SPMV_PIPE_MIN_ROWS and n >= _SPMV_PIPE_MIN_ROWS and A.nnz > 0
+            and A.dtype in (torch.float32, torch.float64)):
+        with torch.cuda.device(dev):
+            return _spmv_pipelined(A, lay, x, alpha, dev)
     xd = _on(x, dev)
     use_y = y is not None and beta != 0.0
     yd = _on(y, dev, A.dtype) if use_y else None
