@@ -423,8 +423,8 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
     ex["config4_block_sparse_attention_bf16"] = {
         "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "blocks_per_head": mask.n_blocks,
         "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 3), "peak": "bf16 measured",
-        "note": "FLOPs counted once per block (QK^T + PV); the kernel's two-pass softmax recomputes QK^T"}
-    # config 4 backward (the survey's first "next" row): dQ, dK, dV on the tensor cores, with the
+        "note": "FLOPs counted once per block (QK^T + PV); one pass with an online softmax"}
+    # config 4 backward: dQ, dK, dV on the tensor cores, with the
     # forward's saved log-sum-exp (as autograd runs it)
     from trnsparse_b200.ops import _attn_backward, _attn_forward
 
