@@ -158,3 +158,42 @@ def test_attention_backward_tc_plan():
                 if ptr[f + 1] == ptr[f]:
                     assert [mode, f, -1, 0] in aux
         assert slots_used == set(range(counts[3]))
+
+
+def test_new_entry_points_validate_before_cuda():
+    """Argument checks of the host-buffer spmv, the format builders and the
+    attention-backward entries run before any CUDA call (no GPU here)."""
+    import torch
+
+    lib = _lib.load()
+    splits = torch.tensor([0, 10], dtype=torch.int64)
+    need = torch.tensor([5], dtype=torch.int64)
+    p = ctypes.c_void_p(1)
+    # n_chunks out of range
+    rc = lib.trnsparse_csr_spmv_host(10, 10, 1, 0, 0, p, p, p, p, 1.0, p, p, p, 0, ctypes.c_void_p(splits.data_ptr()),
+                                     ctypes.c_void_p(need.data_ptr()), None)
+    assert rc == _lib.ERR_ARG and b"n_chunks" in lib.trnsparse_last_error()
+    # row splits that do not span the rows
+    bad = torch.tensor([0, 9], dtype=torch.int64)
+    rc = lib.trnsparse_csr_spmv_host(10, 10, 1, 0, 0, p, p, p, p, 1.0, p, p, p, 1, ctypes.c_void_p(bad.data_ptr()),
+                                     ctypes.c_void_p(need.data_ptr()), None)
+    assert rc == _lib.ERR_ARG and b"row_splits" in lib.trnsparse_last_error()
+    # x_need past n
+    far = torch.tensor([11], dtype=torch.int64)
+    rc = lib.trnsparse_csr_spmv_host(10, 10, 1, 0, 0, p, p, p, p, 1.0, p, p, p, 1, ctypes.c_void_p(splits.data_ptr()),
+                                     ctypes.c_void_p(far.data_ptr()), None)
+    assert rc == _lib.ERR_ARG
+    # format builders: dtype and workspace checks
+    assert lib.trnsparse_bsr_from_dense_count(4, 4, p, 4, _lib.F64, 2, 0.0, p, p, 1 << 20, None) == _lib.ERR_ARG
+    assert lib.trnsparse_bsr_from_dense_count(4, 4, p, 4, _lib.F32, 2, 0.0, p, p, 1, None) == _lib.ERR_ARG
+    assert b"workspace" in lib.trnsparse_last_error()
+    assert lib.trnsparse_csr_from_dense_count(4, 4, p, 2, _lib.F32, 0.0, p, p, 1 << 20, None) == _lib.ERR_ARG
+    assert lib.trnsparse_coo_to_csr(4, 4, 1 << 33, p, p, p, _lib.F32, p, p, p, p, 1 << 40, None) == _lib.ERR_ARG
+    assert _lib.raw("trnsparse_coo_to_csr_workspace_size")(4, 10) >= 8 * 20
+    # attention backward on the tensor cores: shape checks
+    assert lib.trnsparse_bsr_attention_backward_tc(1, 100, 128, p, p, p, p, 0, 0, 0, 0, p, p, p, p, p, None, p, p,
+                                                   p, 1.0, p, 1 << 30, None) == _lib.ERR_ARG
+    assert b"seq" in lib.trnsparse_last_error()
+    assert lib.trnsparse_bsr_attention_backward_tc(1, 128, 96, p, p, p, p, 0, 0, 0, 0, p, p, p, p, p, None, p, p,
+                                                   p, 1.0, p, 1 << 30, None) == _lib.ERR_ARG
+    assert _lib.raw("trnsparse_bsr_attention_backward_tc_workspace_size")(2, 256, 128, 3) == 4 * (2 * 512 + 3 * 2 * 2 * 128 * 128)

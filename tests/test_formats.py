@@ -106,3 +106,15 @@ def test_public_api_matches_reference_names():
     assert sorted(ts.__all__) == sorted(ref)
     for n in ref:
         assert hasattr(ts, n)
+
+
+def test_threshold_rounds_to_the_matrix_dtype():
+    """The device builders compare in the matrix dtype, as torch does with a
+    Python scalar: the float32 0.1 is not > 0.1, the bf16 0.1 is not > 0.1."""
+    from trnsparse_b200.formats import _threshold_in
+
+    for dt in (torch.float32, torch.bfloat16):
+        v = torch.tensor([0.1, 0.2, 1e-3], dtype=dt)
+        for thr in (0.1, 0.15, 1e-3, 0.0, -1.0):
+            t = _threshold_in(dt, thr)
+            assert torch.equal(v.abs() > thr, v.float().abs() > t)
