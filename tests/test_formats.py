@@ -118,3 +118,27 @@ def test_threshold_rounds_to_the_matrix_dtype():
         for thr in (0.1, 0.15, 1e-3, 0.0, -1.0):
             t = _threshold_in(dt, thr)
             assert torch.equal(v.abs() > thr, v.float().abs() > t)
+
+
+def test_spmv_pipeline_plan():
+    """Host plan of the pinned-host spmv pipeline: row chunks of whole 64-row
+    groups covering [0, m), and per chunk the x prefix its columns reach,
+    non-decreasing (a chunk never waits for less than an earlier one)."""
+    from trnsparse_b200 import ops, workloads as w
+
+    A = w.poisson2d_csr(64)  # 4096 rows, band +-64
+    for K in (1, 3, 4, 7):
+        nch, splits, need = ops._spmv_pipe_plan(A.row_ptrs, A.col_indices, A.shape[0], K)
+        s = splits.tolist()
+        assert s[0] == 0 and s[-1] == A.shape[0] and nch == len(s) - 1
+        assert all(b > a and a % 64 == 0 for a, b in zip(s, s[1:]))
+        nd = need.tolist()
+        assert nd == sorted(nd) and nd[-1] == A.shape[1]
+        for i in range(nch):
+            lo, hi = int(A.row_ptrs[s[i]]), int(A.row_ptrs[s[i + 1]])
+            assert nd[i] >= int(A.col_indices[lo:hi].max()) + 1
+    # rows without entries need nothing more than the rows before them
+    E = ts.CSRMatrix(values=torch.ones(2), col_indices=torch.tensor([5, 7]),
+                     row_ptrs=torch.tensor([0, 1] + [1] * 200 + [2]), shape=(202, 10))
+    nch, splits, need = ops._spmv_pipe_plan(E.row_ptrs, E.col_indices, 202, 4)
+    assert need.tolist() == [6, 6, 6, 8][:nch]

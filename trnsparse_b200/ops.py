@@ -78,6 +78,23 @@ _SPMV_PIPE_CHUNKS = 4          # row / x chunks of the host-buffer pipeline (4 m
 _SPMV_PIPE_MIN_ROWS = 1 << 18  # smaller products are not worth splitting
 
 
+def _spmv_pipe_plan(row_ptrs: torch.Tensor, col_indices: torch.Tensor, m: int, K: int):
+    """Row chunks (multiples of 64 rows, about m / K each) and, per chunk, the
+    prefix of x it needs (its largest column + 1, made non-decreasing):
+    ``(n_chunks, splits int64 [n_chunks + 1], need int64 [n_chunks])`` on the host."""
+    rp = row_ptrs.long()
+    rstep = (-(-m // K) + 63) // 64 * 64
+    splits = list(range(0, m, rstep)) + [m]
+    bounds = rp[torch.tensor(splits, device=rp.device)].tolist()
+    need, top = [], 0
+    for i in range(len(splits) - 1):
+        lo, hi = bounds[i], bounds[i + 1]
+        if hi > lo:
+            top = max(top, int(col_indices[lo:hi].max().item()) + 1)
+        need.append(top)
+    return len(splits) - 1, torch.tensor(splits, dtype=torch.int64), torch.tensor(need, dtype=torch.int64)
+
+
 def _spmv_pipelined(A: CSRMatrix, lay: dict, x: torch.Tensor, alpha: float, dev: torch.device) -> torch.Tensor:
     """``alpha * A @ x`` for a pinned host ``x`` through ``trnsparse_csr_spmv_host``:
     x goes up in pieces, each row chunk's product starts once the x entries
@@ -88,18 +105,7 @@ def _spmv_pipelined(A: CSRMatrix, lay: dict, x: torch.Tensor, alpha: float, dev:
     key = ("spmv_pipe", K)
     plan = lay.get(key)
     if plan is None:
-        rp = lay["row_ptrs"].long()
-        ci = lay["col_indices"]
-        rstep = (-(-m // K) + 63) // 64 * 64  # ceil(m / K) rounded up to 64 rows
-        splits = list(range(0, m, rstep)) + [m]
-        bounds = rp[torch.tensor(splits, device=rp.device)].tolist()
-        need, top = [], 0
-        for i in range(len(splits) - 1):
-            lo, hi = bounds[i], bounds[i + 1]
-            if hi > lo:
-                top = max(top, int(ci[lo:hi].max().item()) + 1)
-            need.append(top)
-        plan = (len(splits) - 1, torch.tensor(splits, dtype=torch.int64), torch.tensor(need, dtype=torch.int64))
+        plan = _spmv_pipe_plan(lay["row_ptrs"], lay["col_indices"], m, K)
         lay[key] = plan
     nch, splits, need = plan
     xd = torch.empty(n, dtype=A.dtype, device=dev)
