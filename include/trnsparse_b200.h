@@ -286,8 +286,10 @@ TRNSPARSE_API int trnsparse_bsr_attention_backward(int64_t heads, int64_t seq, i
 
 /* Tensor-core form of trnsparse_bsr_attention for bf16, block size 128,
  * head_dim 64 or 128, seq a multiple of 128: tcgen05 S = Q K^T and O += P V
- * with TMEM accumulators, in the reference's two-pass softmax form (row max
- * and sum over all stored blocks first, then exp(s - max) / sum @ V). */
+ * with TMEM accumulators in one pass (an online softmax whose running max
+ * moves only when a block's max exceeds it by 2^8; numerator and denominator
+ * share it, so O equals the reference's exp(s - max) / sum @ V up to
+ * rounding). */
 TRNSPARSE_API int trnsparse_bsr_attention_tc(int64_t heads, int64_t seq, int64_t head_dim, const int* block_row_ptr,
                                const int* block_col_idx, const void* Q, const void* K, const void* V,
                                void* O, double scale, void* stream);
