@@ -665,17 +665,6 @@ def _attn_forward(Q, K, V, mask_bsr, scale, cuda_cores: bool = False, want_lse: 
     return (O, lse) if want_lse else O
 
 
-def _attn_dense_mask(mask_bsr, seq, dev):
-    b = mask_bsr.block_size
-    mt = seq // b
-    rows = torch.repeat_interleave(torch.arange(mt), (mask_bsr.block_row_ptrs[1:mt + 1] - mask_bsr.block_row_ptrs[:mt]).cpu())
-    bm = torch.zeros(mt, mt, dtype=torch.bool)
-    bm[rows, mask_bsr.block_col_indices[: rows.numel()].long().cpu()] = True
-    m = torch.zeros(seq, seq, dtype=torch.bool)
-    m[: mt * b, : mt * b] = bm.repeat_interleave(b, 0).repeat_interleave(b, 1)
-    return m.to(dev)
-
-
 def _mask_indices(mask_bsr, dev):
     """Block-row pointers / column indices of the mask and its transposed
     pattern (column pointers / row indices), int32 on ``dev``; cached with the
