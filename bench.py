@@ -41,6 +41,12 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
+
+# DRAM bytes per launch measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum,
+# one launch of each kernel on the workload its row reports)
+NCU_TRAFFIC = {
+    "csr_spmv_warp_kernel": 205.3e6,  # config 2 spmv
+}
 METRIC = BASELINE["metric"]
 
 
@@ -263,8 +269,9 @@ def run_ours(args, ws, rank, local):
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(ach / pk["hbm_gbs"], 4), "peak_source": pk["source"] + " (burst copy)",
-                     "traffic": 205.3e6, "traffic_source": "ncu dram__bytes_read+write, one cold launch "
-                     "(profiles/csr_spmv_warp_config2.md)", "kernel": "csr_spmv_warp_kernel<int,float,2,384>"},
+                     "traffic": NCU_TRAFFIC["csr_spmv_warp_kernel"],
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch on this "
+                     "workload (L2 flushed before it)", "kernel": "csr_spmv_warp_kernel<int,float,2,384>"},
         "clocks": clk.summary(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -294,24 +301,63 @@ def run_ours(args, ws, rank, local):
     return line
 
 
+def _gather_x(x_local: torch.Tensor, ws: int) -> torch.Tensor | None:
+    """The full solution on rank 0 (shards are contiguous block-row ranges in rank order)."""
+    if ws == 1:
+        return x_local
+    import torch.distributed as dist
+
+    n = torch.tensor([x_local.numel()], dtype=torch.int64, device=x_local.device)
+    sizes = [torch.zeros_like(n) for _ in range(ws)]
+    dist.all_gather(sizes, n)
+    cap = int(max(int(t.item()) for t in sizes))
+    buf = torch.zeros(cap, dtype=x_local.dtype, device=x_local.device)
+    buf[: x_local.numel()] = x_local
+    parts = [torch.empty_like(buf) for _ in range(ws)]
+    dist.all_gather(parts, buf)
+    return torch.cat([p[: int(t.item())] for p, t in zip(parts, sizes)])
+
+
 def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
                    transports: tuple = ("cgcg", "coop", "fused", "peer", "nccl")) -> dict:
     """Config 5 on ws GPUs: block-row-sharded Jacobi-PCG (strong scaling: the
     2048-block-row matrix is split across the ranks), each transport (cgcg:
     one reduction per iteration in one cooperative launch; coop / fused /
     peer / nccl: the reference's two reductions), whole solve captured in one
-    CUDA graph. 30 iterations, all of which do
-    work (the reference's loop breaks on |p.Ap| < 1e-30 near iteration 31
-    for this matrix); time = max over ranks."""
+    CUDA graph, ``iters`` iterations with tol 0, time = max over ranks.
+
+    Every row carries its own correctness check and speed-up: the sharded x
+    is gathered to rank 0 and compared (relative 2-norm error) with the
+    unsharded single-GPU ``cg_bsr`` solve of the same matrix, right-hand side
+    and iteration count, which rank 0 also times in the same run
+    (``us_per_iteration_single_gpu``); ``speedup_vs_1gpu`` = single-GPU time
+    per iteration / sharded time per iteration."""
     import torch.distributed as dist
 
+    import trnsparse_b200 as ts
     from trnsparse_b200 import distributed as D
     from trnsparse_b200 import workloads as w
 
     A, b = w.block_pentadiagonal_spd()
+    iters = 30
+    # the single-GPU reference solve (rank 0): the library's own cg_bsr with Jacobi
+    single = {}
+    if rank == 0:
+        M = ts.jacobi_preconditioner_bsr(A)
+        bd = b.cuda()
+        ts.cg_bsr(A, bd, tol=0.0, max_iter=iters, M=M)
+        torch.cuda.synchronize()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        x1, it1, rel1 = ts.cg_bsr(A, bd, tol=0.0, max_iter=iters, M=M)
+        e.record()
+        torch.cuda.synchronize()
+        single = {"x": x1.clone(), "ms": a.elapsed_time(e), "rel": rel1}
+        del M, bd
     sh = D.shard_bsr(A, rank, ws)
     bl = b[sh.r0 * 128 : sh.r1 * 128].cuda()
-    iters = 30
+    devs = [None] * ws
+    dist.all_gather_object(devs, str(torch.cuda.get_device_properties(local).uuid))
     out = {}
     for transport in transports:
         try:
@@ -326,15 +372,22 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
             torch.cuda.synchronize()
             ms = max_over_ranks(a.elapsed_time(e), ws)
             executed = cg.executed_iterations()
+            xg = _gather_x(x, ws)
             cg.close()
         except Exception as exc:  # one transport failing must not lose the others' numbers
             out[f"config5_cg_sharded_{transport}"] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
             continue
         nb = A.n_blocks * 128 * 128 * 4
-        out[f"config5_cg_sharded_{transport}"] = {
-            "us_per_iteration": round(ms / max(executed, 1) * 1e3, 2), "iterations": executed,
-            "ranks": ws, "matrix_GB/s_aggregate": round(nb * executed / (ms * 1e-3) / 1e9, 1),
-            "scaling": "strong", "rel_residual": rel}
+        row = {"us_per_iteration": round(ms / max(executed, 1) * 1e3, 2), "executed_iterations": executed,
+               "max_iter": iters, "ranks": ws, "gpus_active": len(set(devs)),
+               "matrix_GB/s_aggregate": round(nb * executed / (ms * 1e-3) / 1e9, 1),
+               "scaling": "strong", "rel_residual": rel}
+        if rank == 0:
+            err = float((xg.double() - single["x"].double()).norm() / single["x"].double().norm())
+            us1 = single["ms"] / max(executed, 1) * 1e3
+            row.update({"rel_err_vs_single_gpu": err, "us_per_iteration_single_gpu": round(us1, 2),
+                        "speedup_vs_1gpu": round(us1 / (ms / max(executed, 1) * 1e3), 3)})
+        out[f"config5_cg_sharded_{transport}"] = row
     return out
 
 
@@ -442,17 +495,22 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
     A5, b5 = w.block_pentadiagonal_spd()
     M5 = ts.jacobi_preconditioner_bsr(A5)
     bd = b5.cuda()
-    ts.cg_bsr(A5, bd, tol=0.0, max_iter=5, M=M5)
+    from trnsparse_b200.iterative import _cg_bsr_device
+
+    _cg_bsr_device(A5, bd, None, 0.0, 5, M5)
     torch.cuda.synchronize()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    x, it, rel = ts.cg_bsr(A5, bd, tol=0.0, max_iter=200, M=M5)
+    x, it, rel, executed = _cg_bsr_device(A5, bd, None, 0.0, 200, M5)
     e.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(e)
-    ex["config5_cg_bsr_jacobi_200"] = {"ms_total": round(ms, 3), "iters_reported": it, "rel_residual": rel,
-                                       "note": "reference semantics stop the work when |p.Ap| < 1e-30 (reported "
-                                               "iters stays max_iter); see bsr_spmv row for per-iteration cost"}
+    ex["config5_cg_bsr_jacobi_200"] = {
+        "ms_total": round(ms, 3), "iters_reported": it, "executed_iterations": executed,
+        "us_per_executed_iteration": round(ms / max(executed, 1) * 1e3, 2), "rel_residual": rel,
+        "note": "tol 0, max_iter 200 with the reference's control flow: the loop breaks when |p.Ap| < 1e-30 "
+                "(iters_reported stays max_iter, as the reference returns); the whole solve is one cooperative "
+                "launch that returns at the break, so ms_total covers the executed iterations only"}
     xv = bd.unsqueeze(1)
     ms = time_call(lambda: ts.bsr_spmm(A5, xv), 10, None)
     nb = A5.n_blocks * 128 * 128 * 4 + 4 * A5.n_blocks + 4 * 2049 + 8 * A5.shape[0]

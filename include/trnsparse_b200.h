@@ -427,9 +427,16 @@ TRNSPARSE_API int trnsparse_bsr_cgcg_solve(int64_t m, int64_t n, int b, int64_t 
  * over [0, max_iter + 1), but its scratch is a fixed 64 MiB array inside the
  * library, held on every GPU that loads the library until exit, instead of a
  * caller workspace; sizes whose trnsparse_bsr_cg_workspace_size exceeds that
- * are rejected with TRNSPARSE_ERR_ARG. The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress); make that first call
- * before any stream capture. All calls share the one array, so calls that
+ * are rejected with TRNSPARSE_ERR_ARG. The array belongs to the library's
+ * device module: the driver creates it (64 MiB) when that module is first
+ * loaded on a device, which, under CUDA's default lazy loading, is the first
+ * call of ANY library function on that device. A caller that must not
+ * allocate later should make one library call per device at start-up (this
+ * entry point included: its first call on a device also looks up the array's
+ * device address with cudaGetSymbolAddress), before any allocator callback
+ * or stream capture. The address is kept per device for the life of the
+ * process; do not call this entry point after cudaDeviceReset, which reloads
+ * the module. All calls share the one array, so calls that
  * overlap on the GPU (other streams, other host threads) race; run them one
  * after another. status_out (nullable, device, 64 bytes) receives the final
  * status record described above. Calls no allocating routine. */
@@ -474,6 +481,43 @@ TRNSPARSE_API size_t trnsparse_coo_to_csr_workspace_size(int64_t m, int64_t nnz)
 TRNSPARSE_API int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const long long* rows,
                          const long long* cols, const void* values, int dtype, long long* row_ptr,
                          long long* cols_out, void* values_out, void* ws, size_t ws_bytes, void* stream);
+
+/* ---- CSR value gradient ------------------------------------------------
+ * out[e] = alpha * sum_t G[row_e, t] * X[col_e, t] over the stored entries e
+ * of A (row_ptrs/col_indices, index_type I32/I64; G m x k, X n x k,
+ * row-major, dtype F32/F64): the adjoint of alpha * A @ X with respect to A's
+ * values. The reference gets it from torch autograd through the
+ * materialised product (nki/dispatch.py:154-178, dA = (dC @ B^T) projected on
+ * the pattern); here it is one sampled dense-dense product over the pattern. */
+TRNSPARSE_API int trnsparse_csr_sddmm(int64_t m, int64_t n, int64_t k, int64_t nnz, int index_type, int dtype,
+                        const void* row_ptrs, const void* col_indices, const void* G, int64_t ldg,
+                        const void* X, int64_t ldx, double alpha, void* out, void* stream);
+
+/* ---- transposes (autograd adjoints and spmv_symmetric) ----------------
+ * Transposed structure of a CSR matrix on the device: the reference builds
+ * A^T through a host COO round trip (trnsparse/ops.py:146-154
+ * sparse_transpose) and the strict triangle of spmv_symmetric through a
+ * coalesced COO tensor (ops.py:81-104). row_ptr/col_idx: index_type I32 or
+ * I64. strict != 0 leaves the diagonal entries out (square A only). Outputs:
+ * row_ptr_t (int64 [n + 1]), col_t (int64, the source row of each entry of
+ * A^T) and perm (int64, the index in A of each entry of A^T); entries of A^T
+ * are ordered by (row of A^T, column of A^T) with the first row_ptr_t[n]
+ * slots of col_t/perm used. No host synchronisation. The values of A^T are
+ * gathered per call with trnsparse_gather (values[perm]), so in-place updates
+ * of A's values never see a stale transpose. The same call on a BSR
+ * matrix's block pointers gives the transposed block pattern. */
+TRNSPARSE_API size_t trnsparse_csr_transpose_workspace_size(int64_t m, int64_t n, int64_t nnz);
+TRNSPARSE_API int trnsparse_csr_transpose(int64_t m, int64_t n, int64_t nnz, int index_type, const void* row_ptr,
+                            const void* col_idx, int strict, long long* row_ptr_t, long long* col_t,
+                            long long* perm, void* ws, size_t ws_bytes, void* stream);
+/* dst[p] = src[idx[p]], elements of 2, 4 or 8 bytes (CSR values of A^T). */
+TRNSPARSE_API int trnsparse_gather(int64_t count, int elem_bytes, const void* src, const long long* idx, void* dst,
+                     void* stream);
+/* dst block p = transpose of src block idx[p], b x b blocks of 2- or 4-byte
+ * elements: the blocks of A^T in its block order (the reference's autograd
+ * transposes every stored block for dB = A^T dC, nki/dispatch.py:331-369). */
+TRNSPARSE_API int trnsparse_bsr_blocks_transpose(int64_t count, int b, int elem_bytes, const void* src,
+                                   const long long* idx, void* dst, void* stream);
 
 #ifdef __cplusplus
 }

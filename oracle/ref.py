@@ -12,6 +12,10 @@ import math
 import torch
 
 __all__ = [
+    "csr_spmm_backward",
+    "bsr_spmm_backward",
+    "screened_spmm_backward",
+    "csr_spmv_symmetric",
     "csr_spmv",
     "csr_spmm",
     "csr_from_dense",
@@ -52,6 +56,18 @@ def csr_spmm(row_ptrs, col_indices, values, shape, B, alpha=1.0, C=None, beta=0.
     if C is not None and beta != 0.0:
         out = out + beta * C
     return out
+
+
+def csr_spmv_symmetric(row_ptrs, col_indices, values, shape, x, alpha=1.0):
+    """trnsparse/ops.py:81-104: alpha * (A @ x + strict(A)^T @ x), strict(A) = the
+    stored entries off the diagonal, summed as a coalesced COO tensor."""
+    m, n = shape
+    assert m == n, "Matrix must be square for symmetric SpMV"
+    rows = torch.repeat_interleave(torch.arange(m), row_ptrs[1:] - row_ptrs[:-1])
+    off = rows != col_indices
+    A = torch.sparse_csr_tensor(row_ptrs, col_indices, values, size=shape)
+    strict = torch.sparse_coo_tensor(torch.stack([rows[off], col_indices[off]]), values[off], size=shape).coalesce()
+    return alpha * (A @ x + strict.t() @ x)
 
 
 def csr_from_dense(A, threshold=0.0):
@@ -148,6 +164,40 @@ def screened_spmm(A, diag_integrals, B, threshold):
 def screened_spmm_pair(A, Q, B, threshold):
     """2-D pair-bound form: (A * screen_quartets(Q, threshold)) @ B (screening.py:29-40)."""
     return (A * screen_quartets(Q, threshold).to(A.dtype)) @ B
+
+
+# --------------------------------------------------------------------------- product adjoints
+def csr_spmm_backward(dense, B, dC):
+    """trnsparse/nki/dispatch.py:154-178 (_SpMMFunction.backward): the dense
+    gradient dC @ B^T of the materialised A (the stored values' gradient is
+    its restriction to A's pattern) and dB = A^T @ dC."""
+    return dC @ B.T, dense.T @ dC
+
+
+def bsr_spmm_backward(blocks, block_col_indices, block_row_ptrs, shape, block_size, B, dC):
+    """trnsparse/nki/dispatch.py:331-369 (_BSRSpMMFunction.backward):
+    dblocks[k] = dC[row block of k] @ B[col block of k]^T per stored block, and
+    dB = A^T @ dC through the materialised dense A."""
+    b = block_size
+    m, n = shape
+    rp = block_row_ptrs.tolist()
+    ci = block_col_indices.tolist()
+    dblocks = torch.zeros_like(blocks)
+    for i in range(len(rp) - 1):
+        for k in range(rp[i], rp[i + 1]):
+            j = ci[k]
+            dblocks[k] = dC[i * b : (i + 1) * b] @ B[j * b : (j + 1) * b].T
+    dense = bsr_to_dense(blocks, block_col_indices, block_row_ptrs, shape, b)
+    return dblocks, dense.T @ dC
+
+
+def screened_spmm_backward(A, diag_integrals, B, threshold, dC):
+    """trnsparse/nki/dispatch.py:447-484 (_ScreenedSpMMFunction.backward), 1-D
+    bounds: mask = sqrt|d_i| sqrt|d_j| > sqrt(threshold);
+    dA = (dC @ B^T) * mask, dB = (A * mask)^T @ dC."""
+    Q = torch.sqrt(torch.abs(diag_integrals))
+    m = ((Q.unsqueeze(-1) * Q.unsqueeze(0)) > math.sqrt(threshold)).to(A.dtype)
+    return (dC @ B.T) * m, (A * m).T @ dC
 
 
 # --------------------------------------------------------------------------- attention

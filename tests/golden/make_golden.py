@@ -84,6 +84,25 @@ add_spmm("spmm_odd_cols_ab", A, torch.randn(90, 7), 0.75, torch.randn(150, 7), -
 A = torch.tensor([[1.0, 0.0, 2.0], [0.0, 0.0, 0.0], [3.0, 4.0, 5.0]])
 cases["nnz_per_row"] = {"op": "nnz_per_row", "dense": A, "out": trnsparse.nnz_per_row(trnsparse.from_dense(A))}
 
+
+# spmv_symmetric: one stored triangle of a symmetric matrix (ops.py:81-104)
+def add_spmv_sym(name, A, x, alpha=1.0):
+    csr = trnsparse.from_dense(A)
+    out = trnsparse.spmv_symmetric(csr, x, alpha=alpha, uplo="upper")
+    cases[name] = {"op": "spmv_symmetric", "dense": A, "csr": csr_dict(csr), "x": x, "alpha": alpha, "out": out}
+
+
+Ak = torch.tensor([[4.0, 1.0, 0.0], [1.0, 3.0, 2.0], [0.0, 2.0, 5.0]])
+add_spmv_sym("spmv_sym_known", torch.triu(Ak), torch.tensor([1.0, 2.0, 3.0]))
+torch.manual_seed(21)
+S = torch.randn(257, 257)
+S[torch.rand(257, 257) > 0.04] = 0.0
+S = torch.triu(S + S.t())
+S[31] = 0.0  # an empty row
+S[100, 100] = 0.0  # a row without its diagonal entry
+add_spmv_sym("spmv_sym_upper", S, torch.randn(257))
+add_spmv_sym("spmv_sym_alpha", S, torch.randn(257), alpha=-0.75)
+
 # ---------------------------------------------------------------- BSR
 def block_random(mb, nb, b, dens, seed):
     torch.manual_seed(seed)
@@ -226,6 +245,58 @@ v0 = torch.randn(128)
 lam_p, v, it = trnsparse.power_iteration_bsr(Ab, v0=v0, max_iter=200, tol=1e-6)
 cases["power"] = {"op": "power", "bsr": bsr_dict(Ab), "v0": v0, "max_iter": 200, "tol": 1e-6, "lam": lam_p, "v": v,
                   "iters": it, "eig_max": lam.max().item()}
+
+# ---------------------------------------------------------------- autograd backward formulas
+# The reference's backward passes live in its autograd Functions
+# (trnsparse/nki/dispatch.py); their forward needs the NKI toolchain, so the
+# backward staticmethods are called directly with a context object holding
+# what the forward would have saved.
+from trnsparse.nki import dispatch as _dispatch  # noqa: E402
+
+
+class _Ctx:
+    def __init__(self, saved, needs, **kw):
+        self.saved_tensors = saved
+        self.needs_input_grad = needs
+        self.__dict__.update(kw)
+
+
+torch.manual_seed(31)
+Db = torch.randn(3 * 128, 2 * 128)
+Db[128:256] = 0.0  # an empty block-row
+Db[0:128, 128:256] = 0.0  # a missing off-diagonal block
+bsr_b = trnsparse.BSRMatrix.from_dense(Db, block_size=128)
+Bb = torch.randn(256, 16)
+dCb = torch.randn(384, 16)
+ctx = _Ctx((bsr_b.blocks, bsr_b.block_col_indices, bsr_b.block_row_ptrs, Bb),
+           (True, False, False, False, False, True), A_shape=bsr_b.shape, A_block_size=128)
+gblk, _, _, _, _, gB = _dispatch._BSRSpMMFunction.backward(ctx, dCb)
+cases["bsr_bwd"] = {"op": "bsr_spmm_backward", "bsr": bsr_dict(bsr_b), "B": Bb, "dC": dCb, "dblocks": gblk, "dB": gB}
+
+torch.manual_seed(32)
+n_s = 256
+r_s = torch.rand(n_s, 3) * 6.0
+diag_s = torch.exp(-0.5 * torch.cdist(r_s, r_s) ** 2).diagonal().clone() * torch.rand(n_s)
+A_s = torch.randn(n_s, n_s)
+B_s = torch.randn(n_s, 24)
+dC_s = torch.randn(n_s, 24)
+Q_s = torch.sqrt(torch.abs(diag_s))
+mask_s = (Q_s.unsqueeze(-1) * Q_s.unsqueeze(0)) > (1e-3) ** 0.5
+ctx = _Ctx((A_s, B_s, mask_s), (True, False, False, True))
+gA, _, _, gB = _dispatch._ScreenedSpMMFunction.backward(ctx, dC_s)
+cases["screened_bwd"] = {"op": "screened_spmm_backward", "A": A_s, "diag": diag_s, "B": B_s, "threshold": 1e-3,
+                         "dC": dC_s, "dA": gA, "dB": gB}
+
+torch.manual_seed(33)
+Dm = torch.randn(200, 137)
+Dm[torch.rand(200, 137) > 0.05] = 0.0
+Bm = torch.randn(137, 24)
+dCm = torch.randn(200, 24)
+ctx = _Ctx((Dm, Bm), (True, True))
+gA, gB = _dispatch._SpMMFunction.backward(ctx, dCm)
+cases["spmm_bwd"] = {"op": "spmm_backward", "dense": Dm, "csr": csr_dict(trnsparse.from_dense(Dm)), "B": Bm,
+                     "dC": dCm, "dA_dense": gA, "dB": gB}
+
 
 def _compact(v):
     if isinstance(v, torch.Tensor):

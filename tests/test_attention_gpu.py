@@ -276,3 +276,30 @@ def test_attention_backward_tensor_core_lse_and_cuda_core_agree():
     for x, y, z in zip(a, b, c):
         assert rel_fro(x.float(), y.float()) <= 1e-2
         assert rel_fro(x.float(), z.float()) <= 1e-2
+
+
+def test_attention_config4_full_size():
+    """The benchmarked shape (config 4: 16 heads x seq 16384 x head_dim 128, bf16,
+    causal window of 8 blocks plus 2 global blocks, 1,235 blocks per head):
+    forward heads 0 and 15 and the backward (dQ, dK, dV) of head 15 against the
+    fp32 oracle on the fp32-upcast inputs, 2e-2 relative Frobenius. The
+    backward splits each global column's 128 partner query blocks into 8
+    units, as the bench runs it."""
+    mask = w.sliding_window_mask()
+    assert mask.n_blocks == 1235 and mask.shape == (16384, 16384)
+    Q, K, V = w.attention_inputs()
+    assert Q.shape == (1, 16, 16384, 128) and Q.dtype == torch.bfloat16
+    dO = torch.randn(Q.shape, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    Qd, Kd, Vd = (t.cuda().requires_grad_(True) for t in (Q, K, V))
+    out = ts.block_sparse_attention_tiled(Qd, Kd, Vd, mask)
+    out.backward(dO.cuda())
+    assert ts._lib.device_error() == 0
+    rp, ci = mask.block_row_ptrs, mask.block_col_indices
+    for h in (0, 15):
+        args = [t[0, h].float() for t in (Q, K, V)]
+        O = oracle.block_sparse_attention(*args, rp, ci, 128)
+        assert rel_fro(out[0, h].detach().float(), O) <= 2e-2, h
+        if h == 15:
+            refs = oracle.block_sparse_attention_backward(*args, O, dO[0, h].float(), rp, ci, 128)
+            for name, got, ref in zip("QKV", (Qd.grad, Kd.grad, Vd.grad), refs):
+                assert rel_fro(got[0, h].float(), ref) <= 2e-2, name

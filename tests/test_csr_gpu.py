@@ -171,3 +171,55 @@ def test_spmv_pinned_host_pipeline(index_dtype):
     xb = torch.randn(n, generator=torch.Generator().manual_seed(9))
     torch.testing.assert_close(ts.spmv(B, xb.pin_memory()), ts.spmv(B, xb.cuda()).cpu(), rtol=1e-6, atol=1e-6)
     assert ts._lib.device_error() == 0
+
+
+# ---------------------------------------------------------------- spmv_symmetric (ops.py:81-104)
+@pytest.mark.parametrize("name", golden_names("spmv_symmetric"))
+def test_spmv_symmetric_golden(name):
+    c = golden_cases()[name]
+    A = _csr(c["csr"], torch.int32)
+    got = ts.spmv_symmetric(A, c["x"].cuda(), alpha=c["alpha"])
+    assert got.is_cuda
+    assert rel_fro(got, c["out"]) <= TOL32
+    host = ts.spmv_symmetric(_csr(c["csr"], device="cpu"), c["x"], alpha=c["alpha"])
+    assert host.device.type == "cpu" and rel_fro(host, c["out"]) <= TOL32
+
+
+def test_spmv_symmetric_sees_in_place_updates():
+    """The strict-triangle transpose caches only the structure: an in-place change
+    of A.values is used by the next call (the reference rebuilds it every call)."""
+    c = golden_cases()["spmv_sym_upper"]
+    d = c["csr"]
+    A = _csr(d, torch.int32)
+    x = c["x"].cuda()
+    ts.spmv_symmetric(A, x)
+    A.values.mul_(-2.0)
+    A.values[::7] += 1.0
+    want = oracle.csr_spmv_symmetric(d["row_ptrs"], d["col_indices"], A.values.cpu(), d["shape"], c["x"])
+    assert rel_fro(ts.spmv_symmetric(A, x), want) <= TOL32
+
+
+def test_csr_transpose_structure_on_device():
+    """trnsparse_csr_transpose gives the stable (column, row) order bit for bit."""
+    from trnsparse_b200 import workloads as w
+    from trnsparse_b200.ops import _transpose_structure
+
+    A = w.poisson2d_csr(64)
+    g = torch.Generator().manual_seed(3)
+    D = torch.randn(300, 211, generator=g) * (torch.rand(300, 211, generator=g) < 0.05)
+    D[:, 17] = 0.0
+    D[40] = torch.randn(211, generator=g)
+    for M, strict in ((A, False), (A, True), (ts.from_dense(D), False)):
+        m, n = M.shape
+        rpt, colt, perm, nnz_t = _transpose_structure(M.row_ptrs, M.col_indices, m, n, strict, {},
+                                                      torch.device("cuda"))
+        rows = torch.repeat_interleave(torch.arange(m), (M.row_ptrs[1:] - M.row_ptrs[:-1]).long())
+        cols = M.col_indices.long()
+        keep = torch.nonzero(rows != cols).squeeze(1) if strict else torch.arange(rows.numel())
+        order = keep[torch.argsort(cols[keep] * m + rows[keep], stable=True)]
+        want_rp = torch.zeros(n + 1, dtype=torch.long)
+        want_rp[1:] = torch.cumsum(torch.bincount(cols[keep], minlength=n), 0)
+        assert nnz_t == order.numel()
+        assert torch.equal(perm.cpu(), order)
+        assert torch.equal(colt.cpu().long(), rows[order])
+        assert torch.equal(rpt.cpu().long(), want_rp)

@@ -46,6 +46,19 @@ def test_spmm_known_answer():
     assert torch.all(golden_cases()["spmm_alpha_beta"]["out"] == 7.0)  # tests/test_ops.py:61-67
 
 
+@pytest.mark.parametrize("name", golden_names("spmv_symmetric"))
+def test_spmv_symmetric(name):
+    c = golden_cases()[name]
+    d = c["csr"]
+    got = oracle.csr_spmv_symmetric(d["row_ptrs"], d["col_indices"], d["values"], d["shape"], c["x"], c["alpha"])
+    torch.testing.assert_close(got, c["out"], atol=0, rtol=0)
+
+
+def test_spmv_symmetric_known_answer():
+    c = golden_cases()["spmv_sym_known"]
+    assert c["out"].tolist() == [6.0, 13.0, 19.0]  # reference tests/test_ops.py:70-79 (A @ x of the full matrix)
+
+
 def test_nnz_per_row_known_answer():
     c = golden_cases()["nnz_per_row"]
     _, _, ptrs = oracle.csr_from_dense(c["dense"])
@@ -146,3 +159,24 @@ def test_attention_backward(name):
                                                         c["block_col_indices"], c["block_size"])
     for got, ref in ((dQ, c["dQ"]), (dK, c["dK"]), (dV, c["dV"])):
         torch.testing.assert_close(got, ref, atol=0, rtol=0)
+
+
+def test_csr_spmm_backward_golden():
+    c = golden_cases()["spmm_bwd"]
+    dA, dB = oracle.csr_spmm_backward(c["dense"], c["B"], c["dC"])
+    torch.testing.assert_close(dA, c["dA_dense"], atol=0, rtol=0)
+    torch.testing.assert_close(dB, c["dB"], atol=0, rtol=0)
+
+
+def test_bsr_spmm_backward_golden():
+    c = golden_cases()["bsr_bwd"]
+    dblk, dB = oracle.bsr_spmm_backward(*_bsr(c), c["B"], c["dC"])
+    torch.testing.assert_close(dblk, c["dblocks"], atol=0, rtol=0)
+    torch.testing.assert_close(dB, c["dB"], atol=0, rtol=0)
+
+
+def test_screened_spmm_backward_golden():
+    c = golden_cases()["screened_bwd"]
+    dA, dB = oracle.screened_spmm_backward(c["A"], c["diag"], c["B"], c["threshold"], c["dC"])
+    torch.testing.assert_close(dA, c["dA"], atol=0, rtol=0)
+    torch.testing.assert_close(dB, c["dB"], atol=0, rtol=0)

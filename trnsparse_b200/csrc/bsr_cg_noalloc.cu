@@ -27,7 +27,9 @@ std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {nullptr};
 
 // Device address of the scratch array on the current device (looked up once
-// per device, with that device current).
+// per device, with that device current, and kept for the life of the process:
+// after a cudaDeviceReset the library's device module is loaded again and the
+// array may move, so the entry point must not be used after a reset).
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -640,6 +640,54 @@ int launch_spmm(int64_t m, int64_t k, int64_t nnz, const void* rp, const void* c
   return TRNSPARSE_OK;
 }
 
+// ---------------------------------------------------------------- SDDMM (value gradient)
+// out[e] = alpha * <G[row_e, :k], X[col_e, :k]> for every stored entry e: the
+// adjoint of alpha * A @ X with respect to A's values, projected on A's pattern.
+// A warp per row. Short k: lanes take entries (each a full dot product, the
+// G row read once per warp from L1); long k: lanes split the dot product and
+// reduce by shuffles. Accumulates in the value type.
+template <typename I, typename T>
+__global__ void __launch_bounds__(256)
+csr_sddmm_kernel(int64_t m, int64_t k, const I* __restrict__ row_ptrs, const I* __restrict__ col_indices,
+                 const T* __restrict__ G, int64_t ldg, const T* __restrict__ X, int64_t ldx, T alpha,
+                 T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const int64_t e0 = static_cast<int64_t>(row_ptrs[r]), e1 = static_cast<int64_t>(row_ptrs[r + 1]);
+    const T* g = G + r * ldg;
+    if (k < 16) {
+      for (int64_t e = e0 + lane; e < e1; e += 32) {
+        const T* x = X + static_cast<int64_t>(col_indices[e]) * ldx;
+        T acc = T(0);
+        for (int64_t t = 0; t < k; ++t) acc += g[t] * x[t];
+        out[e] = alpha * acc;
+      }
+    } else {
+      for (int64_t e = e0; e < e1; ++e) {
+        const T* x = X + static_cast<int64_t>(col_indices[e]) * ldx;
+        T acc = T(0);
+        for (int64_t t = lane; t < k; t += 32) acc += g[t] * x[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) out[e] = alpha * acc;
+      }
+    }
+  }
+}
+
+template <typename I, typename T>
+int launch_sddmm(int64_t m, int64_t k, const void* rp, const void* ci, const void* G, int64_t ldg, const void* X,
+                 int64_t ldx, double alpha, void* out, cudaStream_t st) {
+  const int64_t blocks = (m + 7) / 8;
+  const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
+  csr_sddmm_kernel<I, T><<<grid, 256, 0, st>>>(m, k, static_cast<const I*>(rp), static_cast<const I*>(ci),
+                                               static_cast<const T*>(G), ldg, static_cast<const T*>(X), ldx,
+                                               static_cast<T>(alpha), static_cast<T*>(out));
+  TSB_CHECK_LAUNCH("csr_sddmm");
+  return TRNSPARSE_OK;
+}
+
 }  // namespace
 }  // namespace tsb
 
@@ -803,4 +851,24 @@ extern "C" int trnsparse_csr_spmm(int64_t m, int64_t n, int64_t k, int64_t nnz, 
     return fail(TRNSPARSE_ERR_DTYPE, "csr_spmm: dtype %d not supported (F32, F64)", dtype);
   }
   return fail(TRNSPARSE_ERR_DTYPE, "csr_spmm: index type %d not supported (I32, I64)", index_type);
+}
+
+extern "C" int trnsparse_csr_sddmm(int64_t m, int64_t n, int64_t k, int64_t nnz, int index_type, int dtype,
+                                   const void* row_ptrs, const void* col_indices, const void* G, int64_t ldg,
+                                   const void* X, int64_t ldx, double alpha, void* out, void* stream) {
+  TSB_REQUIRE(m >= 0 && n >= 0 && k >= 1 && nnz >= 0, "csr_sddmm: bad sizes");
+  if (m == 0 || nnz == 0) return TRNSPARSE_OK;
+  TSB_REQUIRE(row_ptrs && col_indices && G && X && out, "csr_sddmm: null pointer");
+  TSB_REQUIRE(ldg >= k && ldx >= k, "csr_sddmm: leading dimension smaller than k");
+  cudaStream_t st = as_stream(stream);
+  if (dtype == TRNSPARSE_F32) {
+    if (index_type == TRNSPARSE_I32) return launch_sddmm<int32_t, float>(m, k, row_ptrs, col_indices, G, ldg, X, ldx, alpha, out, st);
+    if (index_type == TRNSPARSE_I64) return launch_sddmm<int64_t, float>(m, k, row_ptrs, col_indices, G, ldg, X, ldx, alpha, out, st);
+  } else if (dtype == TRNSPARSE_F64) {
+    if (index_type == TRNSPARSE_I32) return launch_sddmm<int32_t, double>(m, k, row_ptrs, col_indices, G, ldg, X, ldx, alpha, out, st);
+    if (index_type == TRNSPARSE_I64) return launch_sddmm<int64_t, double>(m, k, row_ptrs, col_indices, G, ldg, X, ldx, alpha, out, st);
+  } else {
+    return fail(TRNSPARSE_ERR_DTYPE, "csr_sddmm: dtype %d not supported (F32, F64)", dtype);
+  }
+  return fail(TRNSPARSE_ERR_DTYPE, "csr_sddmm: index type %d not supported (I32, I64)", index_type);
 }

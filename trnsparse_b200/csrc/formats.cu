@@ -333,12 +333,14 @@ __global__ void csr_fill_kernel(int64_t m, int64_t n, const T* __restrict__ A, i
 }
 
 // ---------------------------------------------------------------- COO -> CSR
+// skip_negative: a row index of -1 marks an entry left out (the strict-triangle transpose)
 __global__ void coo_count_kernel(int64_t nnz, int64_t m, int64_t n, const long long* __restrict__ rows,
                                  const long long* __restrict__ cols, unsigned long long* __restrict__ v,
-                                 int* __restrict__ bad) {
+                                 int* __restrict__ bad, int skip_negative = 0) {
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < nnz;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const long long r = rows[e], c = cols[e];
+    if (skip_negative && r < 0) continue;
     if (r < 0 || r >= m || c < 0 || c >= n) {
       atomicExch(bad, 1);
       continue;
@@ -380,7 +382,9 @@ __device__ __forceinline__ void coo_emit(unsigned long long key, long long p, co
                                          int esz, long long* __restrict__ cols_out, uint8_t* __restrict__ vals_out) {
   cols_out[p] = static_cast<long long>(key >> 32);
   const long long src = static_cast<long long>(key & 0xffffffffull);
-  if (esz == 4)
+  if (vals_in == nullptr)  // no values: emit the source entry index (a permutation)
+    reinterpret_cast<long long*>(vals_out)[p] = src;
+  else if (esz == 4)
     reinterpret_cast<uint32_t*>(vals_out)[p] = reinterpret_cast<const uint32_t*>(vals_in)[src];
   else if (esz == 2)
     reinterpret_cast<uint16_t*>(vals_out)[p] = reinterpret_cast<const uint16_t*>(vals_in)[src];
@@ -527,6 +531,56 @@ __global__ void __launch_bounds__(kSortThreads) coo_sort_long_kernel(
       dst = tmp;
     }
     for (long long t = threadIdx.x; t < len; t += blockDim.x) coo_emit(src[t], b0 + t, vals_in, esz, cols_out, vals_out);
+  }
+}
+
+// CSR transpose, step 1: every entry's transposed coordinates (row = its column,
+// column = its row; row -1 for a diagonal entry when only the strict triangle is kept).
+// A warp per row.
+template <typename I>
+__global__ void csr_entry_coords_kernel(int64_t m, const I* __restrict__ row_ptr, const I* __restrict__ col_idx,
+                                        int strict, long long* __restrict__ trow, long long* __restrict__ tcol) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const int64_t e0 = static_cast<int64_t>(row_ptr[r]), e1 = static_cast<int64_t>(row_ptr[r + 1]);
+    for (int64_t e = e0 + lane; e < e1; e += 32) {
+      const long long c = static_cast<long long>(col_idx[e]);
+      trow[e] = (strict && c == r) ? -1 : c;
+      tcol[e] = r;
+    }
+  }
+}
+
+// dst[p] = src[idx[p]] for elements of 2, 4 or 8 bytes
+template <typename T>
+__global__ void gather_kernel(int64_t count, const T* __restrict__ src, const long long* __restrict__ idx,
+                              T* __restrict__ dst) {
+  for (int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < count;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[p] = src[idx[p]];
+}
+
+// dst block p = (src block idx[p])^T for b x b blocks, through 32 x 33 shared-memory tiles:
+// a CTA per (block, 32 x 32 tile), coalesced reads and writes.
+template <typename T>
+__global__ void block_transpose_gather_kernel(int b, const T* __restrict__ src, const long long* __restrict__ idx,
+                                              T* __restrict__ dst) {
+  __shared__ T tile[32][33];
+  const int tiles = (b + 31) / 32;
+  const int64_t p = blockIdx.y;
+  const int ti = blockIdx.x / tiles, tj = blockIdx.x % tiles;  // source tile (row ti, column tj)
+  const T* s = src + static_cast<int64_t>(idx[p]) * b * b;
+  T* d = dst + p * static_cast<int64_t>(b) * b;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (int y = ty; y < 32; y += 8) {
+    const int r = ti * 32 + y, c = tj * 32 + tx;
+    if (r < b && c < b) tile[y][tx] = s[static_cast<int64_t>(r) * b + c];
+  }
+  __syncthreads();
+  for (int y = ty; y < 32; y += 8) {
+    const int r = tj * 32 + y, c = ti * 32 + tx;  // destination row = source column
+    if (r < b && c < b) d[static_cast<int64_t>(r) * b + c] = tile[tx][y];
   }
 }
 
@@ -750,4 +804,105 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
   if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: status");
   TSB_REQUIRE(!hbad, "coo_to_csr: a row or column index is out of range");
   return TRNSPARSE_OK;
+}
+
+// ---------------------------------------------------------------- transposes
+extern "C" size_t trnsparse_csr_transpose_workspace_size(int64_t m, int64_t n, int64_t nnz) {
+  if (m < 0 || n < 0 || nnz < 0) return 0;
+  return trnsparse_coo_to_csr_workspace_size(n, nnz) + 2 * sizeof(long long) * (size_t)nnz + 256;
+}
+
+extern "C" int trnsparse_csr_transpose(int64_t m, int64_t n, int64_t nnz, int index_type, const void* row_ptr,
+                                       const void* col_idx, int strict, long long* row_ptr_t, long long* col_t,
+                                       long long* perm, void* ws, size_t ws_bytes, void* stream) {
+  TSB_REQUIRE(m >= 0 && n >= 0 && nnz >= 0, "csr_transpose: bad sizes");
+  TSB_REQUIRE(nnz < (1ll << 32) && m < (1ll << 31), "csr_transpose: nnz must be < 2^32 and m < 2^31");
+  TSB_REQUIRE(index_type == TRNSPARSE_I32 || index_type == TRNSPARSE_I64, "csr_transpose: bad index type");
+  TSB_REQUIRE(!strict || m == n, "csr_transpose: the strict triangle needs a square matrix");
+  TSB_REQUIRE(row_ptr && row_ptr_t && ws, "csr_transpose: null pointer");
+  TSB_REQUIRE(nnz == 0 || (col_idx && col_t && perm), "csr_transpose: null pointer");
+  TSB_REQUIRE(ws_bytes >= trnsparse_csr_transpose_workspace_size(m, n, nnz), "csr_transpose: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  long long* trow = static_cast<long long*>(ws);
+  long long* tcol = trow + nnz;
+  uint8_t* cws = reinterpret_cast<uint8_t*>(tcol + nnz);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(cws);
+  unsigned long long* keys2 = keys + nnz;
+  unsigned long long* cursor = keys2 + nnz;
+  long long* part = reinterpret_cast<long long*>(cursor + n + 1);
+  long long* mid_rows = reinterpret_cast<long long*>(reinterpret_cast<uint8_t*>(part) + scan_ws_bytes(n));
+  long long* long_rows = mid_rows + n;
+  unsigned long long* n_mid = reinterpret_cast<unsigned long long*>(long_rows + n);
+  unsigned long long* n_long = n_mid + 1;
+  int* bad = reinterpret_cast<int*>(n_long + 1);
+  cudaError_t e = cudaMemsetAsync(row_ptr_t, 0, sizeof(long long) * (n + 1), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(n_mid, 0, 24, st);
+  if (e != cudaSuccess) return cuda_status(e, "csr_transpose: clear");
+  if (nnz > 0 && m > 0) {
+    if (index_type == TRNSPARSE_I32)
+      csr_entry_coords_kernel<int><<<grid_for(m, 8), 256, 0, st>>>(m, static_cast<const int*>(row_ptr),
+                                                                   static_cast<const int*>(col_idx), strict, trow, tcol);
+    else
+      csr_entry_coords_kernel<long long><<<grid_for(m, 8), 256, 0, st>>>(
+          m, static_cast<const long long*>(row_ptr), static_cast<const long long*>(col_idx), strict, trow, tcol);
+    coo_count_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, n, m, trow, tcol,
+                                                        reinterpret_cast<unsigned long long*>(row_ptr_t), bad, 1);
+    TSB_CHECK_LAUNCH("csr_transpose: count");
+  }
+  int rc = exclusive_scan(row_ptr_t, n, part, st);
+  if (rc) return rc;
+  if (nnz == 0 || n == 0 || m == 0) return TRNSPARSE_OK;
+  e = cudaMemcpyAsync(cursor, row_ptr_t, sizeof(long long) * n, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return cuda_status(e, "csr_transpose: cursors");
+  coo_scatter_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, n, m, trow, tcol, cursor, keys);
+  coo_sort_tiny_kernel<<<grid_for(n, 256), 256, 0, st>>>(n, row_ptr_t, keys, nullptr, 8, col_t, (uint8_t*)perm,
+                                                        mid_rows, n_mid, long_rows, n_long);
+  coo_sort_mid_kernel<<<grid_for(n, 8), 256, 0, st>>>(row_ptr_t, mid_rows, n_mid, keys, nullptr, 8, col_t,
+                                                     (uint8_t*)perm);
+  coo_sort_long_kernel<<<grid_for(n, 1), kSortThreads, 0, st>>>(row_ptr_t, long_rows, n_long, keys, keys2, nullptr,
+                                                               8, col_t, (uint8_t*)perm);
+  TSB_CHECK_LAUNCH("csr_transpose: sort");
+  return TRNSPARSE_OK;
+}
+
+extern "C" int trnsparse_gather(int64_t count, int elem_bytes, const void* src, const long long* idx, void* dst,
+                                void* stream) {
+  TSB_REQUIRE(count >= 0, "gather: bad count");
+  TSB_REQUIRE(elem_bytes == 2 || elem_bytes == 4 || elem_bytes == 8, "gather: element size must be 2, 4 or 8");
+  if (count == 0) return TRNSPARSE_OK;
+  TSB_REQUIRE(src && idx && dst, "gather: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const int g = grid_for(count, 256);
+  if (elem_bytes == 2)
+    gather_kernel<uint16_t><<<g, 256, 0, st>>>(count, (const uint16_t*)src, idx, (uint16_t*)dst);
+  else if (elem_bytes == 4)
+    gather_kernel<uint32_t><<<g, 256, 0, st>>>(count, (const uint32_t*)src, idx, (uint32_t*)dst);
+  else
+    gather_kernel<uint64_t><<<g, 256, 0, st>>>(count, (const uint64_t*)src, idx, (uint64_t*)dst);
+  TSB_CHECK_LAUNCH("gather");
+  return TRNSPARSE_OK;
+}
+
+extern "C" int trnsparse_bsr_blocks_transpose(int64_t count, int b, int elem_bytes, const void* src,
+                                              const long long* idx, void* dst, void* stream) {
+  TSB_REQUIRE(count >= 0 && b > 0, "bsr_blocks_transpose: bad sizes");
+  TSB_REQUIRE(count < 65536 * 1024ll, "bsr_blocks_transpose: too many blocks");
+  TSB_REQUIRE(elem_bytes == 2 || elem_bytes == 4, "bsr_blocks_transpose: element size must be 2 or 4");
+  if (count == 0) return TRNSPARSE_OK;
+  TSB_REQUIRE(src && idx && dst, "bsr_blocks_transpose: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const int tiles = (b + 31) / 32;
+  int rc = TRNSPARSE_OK;
+  for (int64_t c0 = 0; c0 < count && rc == TRNSPARSE_OK; c0 += 65535) {  // grid.y is at most 65535
+    const int64_t c = count - c0 < 65535 ? count - c0 : 65535;
+    dim3 grid(tiles * tiles, static_cast<unsigned>(c));
+    if (elem_bytes == 2)
+      block_transpose_gather_kernel<uint16_t><<<grid, 256, 0, st>>>(b, (const uint16_t*)src, idx + c0,
+                                                                     (uint16_t*)dst + c0 * b * b);
+    else
+      block_transpose_gather_kernel<uint32_t><<<grid, 256, 0, st>>>(b, (const uint32_t*)src, idx + c0,
+                                                                     (uint32_t*)dst + c0 * b * b);
+    TSB_CHECK_LAUNCH("bsr_blocks_transpose");
+  }
+  return rc;
 }

@@ -96,36 +96,107 @@ def cg_bsr(
 
     Returns ``(x, iters, rel_residual)``; ``x`` is on ``b``'s device.
     """
+    x, iters, rel, _ = _cg_bsr_device(A, b, x0, tol, max_iter, M)
+    return x, iters, rel
+
+
+def _inv_diag_on(M, dev: torch.device) -> torch.Tensor:
+    """The Jacobi preconditioner's inverse diagonal as float32 on ``dev``,
+    copied once per device and kept on the callable (the callable is built
+    for one matrix; its inverse diagonal never changes)."""
+    cache = M.__dict__.setdefault("_trnsparse_inv_d_dev", {})
+    t = cache.get(str(dev))
+    if t is None:
+        t = cache[str(dev)] = _on(M._trnsparse_inv_d, dev, torch.float32)
+    return t
+
+
+def _cg_executed(ws: torch.Tensor, n: int, max_iter: int) -> int:
+    """Iterations that did work: the last k whose p.Ap slot was written (the
+    reference's loop may break early on |p.Ap| < 1e-30)."""
+    import ctypes
+
+    offs = (ctypes.c_size_t * 9)()
+    _lib.call("trnsparse_bsr_cg_layout", n, max_iter, offs)
+    pap = ws[offs[1] : offs[1] + 32 * (max_iter + 1)].view(torch.float64).view(-1, 4)[:, 0]
+    nz = (pap != 0).nonzero()
+    return int(nz[-1].item()) + 1 if nz.numel() else 0
+
+
+def _cg_bsr_device(A, b, x0, tol, max_iter, M) -> tuple[torch.Tensor, int, float, int]:
+    """cg_bsr plus the number of iterations that did work (-1 on the host loop).
+
+    Block size 128, square block-aligned A, x0 = 0: the whole solve is one
+    cooperative launch (``trnsparse_bsr_cg_fused_start`` + ``_coop_run`` on a
+    one-rank peer world whose buffer is a plain workspace): every iteration's
+    two phases run inside the kernel and it returns once the reference's loop
+    would have stopped (converged, or |p.Ap| < 1e-30), so no launch is spent
+    after the end. The arithmetic is that of the two-launch iteration. Other
+    shapes, or an x0, go through ``trnsparse_bsr_cg_start`` / ``_iterate``.
+    """
     inv_d = None
     fused = M is None or (callable(M) and hasattr(M, "_trnsparse_inv_d"))
     if not fused or b.dtype != torch.float32 or A.dtype != torch.float32:
-        return _cg_host_loop(A, b, x0, tol, max_iter, M)
+        x, it, rel = _cg_host_loop(A, b, x0, tol, max_iter, M)
+        return x, it, rel, -1
     dev = _dev_of(b, x0)
     n = b.shape[0]
     geo = _bsr_geometry(A, dev)
     if M is not None:
-        inv_d = _on(M._trnsparse_inv_d, dev, torch.float32)
+        inv_d = _inv_diag_on(M, dev)
     bd = _on(b, dev, torch.float32)
     x = (x0.to(device=dev, dtype=torch.float32).clone() if x0 is not None
          else torch.zeros(n, dtype=torch.float32, device=dev))
     ws_bytes = _lib.raw("trnsparse_bsr_cg_workspace_size")(n, max_iter)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     s = _lib.stream_handle(dev)
+    m_, n_ = A.shape
+    whole = x0 is None and A.block_size == 128 and m_ == n_ == n and n % 128 == 0 and max_iter >= 1
     with torch.cuda.device(dev):
+        if whole:
+            comm_off = (ws_bytes + 255) // 256 * 256
+            ws = torch.zeros(comm_off + _lib.raw("trnsparse_peer_comm_bytes")(1), dtype=torch.uint8, device=dev)
+            peers = torch.full((1,), ws.data_ptr(), dtype=torch.int64, device=dev)  # a fill, no host copy
+            sends = torch.zeros(3, dtype=torch.int64, device=dev)
+            peer = (peers.data_ptr(), 1, 0, comm_off, sends.data_ptr(), 0)
+            _lib.call("trnsparse_bsr_cg_fused_start", n, n, 128, bd.data_ptr(), _lib.ptr(inv_d), max_iter,
+                      ws.data_ptr(), ws_bytes, *peer, s)
+            _lib.call("trnsparse_bsr_cg_coop_run", *geo, x.data_ptr(), _lib.ptr(inv_d), float(tol), max_iter, 0,
+                      max_iter, ws.data_ptr(), *peer, s)
+            done, iters, reason, rel = _status(ws)
+            if reason == 5:
+                raise RuntimeError("cg_bsr: a bounded device wait timed out (device error word set)")
+            return _back(x, b), iters, rel, _cg_executed(ws, n, max_iter)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         _lib.call("trnsparse_bsr_cg_start", *geo, bd.data_ptr(), x.data_ptr(), 1 if x0 is None else 0,
                   _lib.ptr(inv_d), max_iter, ws.data_ptr(), ws_bytes, s)
-        k = 0
-        chunk = max_iter + 1 if tol <= 0 else 16
+        # Iterations go out in chunks; the host reads the status record of a
+        # chunk (an async copy into pinned memory) while the next chunk is
+        # already queued, so the device never waits for the host and at most
+        # one chunk of launches is issued after the solve has ended (they exit
+        # at once on the status word).
+        head = torch.empty(_STATUS_BYTES, dtype=torch.uint8, pin_memory=True)
+        stream = torch.cuda.current_stream(dev)
+        k, chunk = 0, 8
+
+        def launch(k0: int) -> int:
+            k1 = min(k0 + chunk, max_iter + 1)
+            _lib.call("trnsparse_bsr_cg_iterate", *geo, x.data_ptr(), _lib.ptr(inv_d), float(tol), max_iter, k0,
+                      k1, ws.data_ptr(), s)
+            return k1
+
+        k = launch(k)
         while True:
-            k_end = min(k + chunk, max_iter + 1)
-            _lib.call("trnsparse_bsr_cg_iterate", *geo, x.data_ptr(), _lib.ptr(inv_d), float(tol), max_iter, k, k_end,
-                      ws.data_ptr(), s)
-            k = k_end
-            done, iters, _reason, rel = _status(ws)
-            if done or k > max_iter:
+            head.copy_(ws[:_STATUS_BYTES], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            if k <= max_iter:
+                k = launch(k)
+            ev.synchronize()
+            if head[:4].view(torch.int32).item() or k > max_iter:
                 break
-            chunk *= 2
-    return _back(x, b), iters, rel
+            chunk = min(2 * chunk, 64)
+        done, iters, _reason, rel = _status(ws)
+    return _back(x, b), iters, rel, _cg_executed(ws, n, max_iter)
 
 
 def _cg_host_loop(A, b, x0, tol, max_iter, M):

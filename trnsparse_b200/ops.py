@@ -190,29 +190,73 @@ def _spmm_impl(A: CSRMatrix, B: torch.Tensor, alpha: float, C, beta: float) -> t
     return _back(out, B)
 
 
+def _transpose_structure(row_ptrs: torch.Tensor, col_indices: torch.Tensor, m: int, n: int, strict: bool,
+                         cache: dict, dev: torch.device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
+    """Transposed pattern of an m x n CSR structure, built on the device
+    (``trnsparse_csr_transpose``): ``(row_ptr_t, col_t, perm, nnz_t)`` with
+    ``perm`` the index in A of each entry of A^T (the diagonal left out when
+    ``strict``). Index arrays are int32 when the sizes allow. ``cache`` keeps
+    one entry per (strict, device), keyed by the structure's fingerprint and
+    replaced when the structure changes; values are never cached."""
+    from .formats import _fingerprint
+
+    key = ("transpose_structure", strict, str(dev))
+    fp = _fingerprint(col_indices, row_ptrs)
+    hit = cache.get(key)
+    if hit is not None and hit[0] == fp:
+        return hit[1]
+    idx_t = torch.int32 if row_ptrs.dtype == torch.int32 and col_indices.dtype == torch.int32 else torch.int64
+    rp = row_ptrs.to(device=dev, dtype=idx_t).contiguous()
+    ci = col_indices.to(device=dev, dtype=idx_t).contiguous()
+    nnz = ci.numel()
+    rpt = torch.empty(n + 1, dtype=torch.int64, device=dev)
+    colt = torch.empty(max(nnz, 1), dtype=torch.int64, device=dev)
+    perm = torch.empty(max(nnz, 1), dtype=torch.int64, device=dev)
+    ws_bytes = _lib.raw("trnsparse_csr_transpose_workspace_size")(m, n, nnz)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_csr_transpose", m, n, nnz, _lib.index_code(idx_t), rp.data_ptr(), ci.data_ptr(),
+                  1 if strict else 0, rpt.data_ptr(), colt.data_ptr(), perm.data_ptr(), ws.data_ptr(), ws_bytes,
+                  _lib.stream_handle(dev))
+    nnz_t = int(rpt[n].item()) if strict else nnz
+    colt, perm = colt[:nnz_t], perm[:nnz_t]
+    if max(m, nnz_t) < (1 << 31):  # int32 indices halve the index traffic of the transposed products
+        rpt, colt = rpt.to(torch.int32), colt.to(torch.int32)
+    out = (rpt, colt, perm, nnz_t)
+    cache[key] = (fp, out)
+    return out
+
+
+def _gather(src: torch.Tensor, perm: torch.Tensor) -> torch.Tensor:
+    """``src[perm]`` on the device with the library's gather kernel."""
+    out = torch.empty(perm.numel(), dtype=src.dtype, device=src.device)
+    if perm.numel():
+        with torch.cuda.device(src.device):
+            _lib.call("trnsparse_gather", perm.numel(), src.element_size(), src.data_ptr(), perm.data_ptr(),
+                      out.data_ptr(), _lib.stream_handle(src.device))
+    return out
+
+
 def spmv_symmetric(A: CSRMatrix, x: torch.Tensor, alpha: float = 1.0, uplo: str = "upper") -> torch.Tensor:
     """``alpha * (A @ x + strict(A)^T @ x)`` for one stored triangle (ops.py:81-104).
 
-    Both products run through the CSR SpMV kernel; the transpose of the
-    strict triangle is built once on the host (structure only).
+    As in the reference, ``uplo`` does not change the arithmetic: the stored
+    entries are A, the off-diagonal ones are mirrored. The transposed strict
+    pattern is built once per structure on the device; its values are
+    gathered from ``A.values`` on every call (in-place updates of the values
+    are always seen). Both products run through the CSR SpMV kernel: the
+    first gives ``alpha * A @ x``, the second adds ``alpha * strict(A)^T @ x``
+    to it as its ``beta * y`` term.
     """
     m, n = A.shape
     assert m == n, "Matrix must be square for symmetric SpMV"
-    key = ("strict_T",) + tuple(A.row_ptrs.shape)
-    cached = A._dev.get(key)
-    if cached is None or cached[0] is not A.values:
-        coo = A.to_coo()
-        keep = coo.row_indices.cpu() != coo.col_indices.cpu()
-        strict_t = COOMatrix(
-            values=coo.values.cpu()[keep],
-            row_indices=coo.col_indices.cpu()[keep].to(torch.long),
-            col_indices=coo.row_indices.cpu()[keep].to(torch.long),
-            shape=(n, m),
-        ).to_csr()
-        cached = (A.values, strict_t)
-        A._dev[key] = cached
-    strict_t = cached[1]
-    return spmv(A, x, alpha=alpha) + spmv(strict_t, x, alpha=alpha)
+    dev = _dev_of(x)
+    lay = A.device_layout(dev)
+    rpt, colt, perm, nnz_t = _transpose_structure(A.row_ptrs, A.col_indices, m, n, True, A._dev, dev)
+    ST = CSRMatrix(values=_gather(lay["values"], perm), col_indices=colt, row_ptrs=rpt, shape=(n, m))
+    xd = _on(x, dev)
+    y = _spmv_impl(A, xd, alpha, None, 0.0)
+    return _back(_spmv_impl(ST, xd, alpha, y, 1.0), x)
 
 
 def sparse_add(A: CSRMatrix, B: CSRMatrix, alpha: float = 1.0, beta: float = 1.0) -> CSRMatrix:
@@ -374,43 +418,30 @@ def _needs_grad(*ts) -> bool:
     return torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in ts)
 
 
-def _csr_transpose(A: CSRMatrix) -> tuple[CSRMatrix, torch.Tensor]:
-    """A^T as a CSRMatrix and, for each of its entries, the index of the entry of A
-    it came from (cached per A's fingerprint)."""
-    from .formats import _fingerprint
-
-    key = ("transpose", _fingerprint(A.values, A.col_indices, A.row_ptrs))
-    hit = A._dev.get(key)
-    if hit is not None:
-        return hit
+def _csr_transpose(A: CSRMatrix, dev: torch.device) -> CSRMatrix:
+    """A^T as a CSRMatrix on ``dev``: the transposed structure (built on the
+    device once per structure, one cache slot per matrix) and the values
+    gathered from A's current values on every call."""
     m, n = A.shape
-    rp = A.row_ptrs.to(torch.long).cpu()
-    ci = A.col_indices.to(torch.long).cpu()
-    rows = torch.repeat_interleave(torch.arange(m), rp[1:] - rp[:-1])
-    order = torch.argsort(ci * max(m, 1) + rows, stable=True)
-    rpt = torch.zeros(n + 1, dtype=torch.long)
-    rpt[1:] = torch.cumsum(torch.bincount(ci, minlength=n)[:n], 0)
-    idx_t = A.row_ptrs.dtype if A.row_ptrs.dtype == A.col_indices.dtype else torch.long
-    AT = CSRMatrix(values=A.values.detach()[order.to(A.values.device)], col_indices=rows[order].to(idx_t),
-                   row_ptrs=rpt.to(idx_t), shape=(n, m))
-    A._dev[key] = (AT, order)
-    return AT, order
+    rpt, colt, perm, _ = _transpose_structure(A.row_ptrs, A.col_indices, m, n, False, A._dev, dev)
+    vals = A.device_layout(dev)["values"]
+    return CSRMatrix(values=_gather(vals, perm), col_indices=colt, row_ptrs=rpt, shape=(n, m))
 
 
 def _csr_values_grad(A: CSRMatrix, dC: torch.Tensor, B: torch.Tensor, alpha: float) -> torch.Tensor:
-    """d values[j] = alpha * <dC[row_j], B[col_j]> (the product's adjoint projected on A's pattern)."""
-    dev = dC.device
-    rp = A.row_ptrs.to(device=dev, dtype=torch.long)
-    rows = torch.repeat_interleave(torch.arange(A.shape[0], device=dev), rp[1:] - rp[:-1])
-    cols = A.col_indices.to(device=dev, dtype=torch.long)
-    dC2 = dC.reshape(dC.shape[0], -1)
-    B2 = B.to(dev).reshape(B.shape[0], -1)
-    out = torch.empty(A.nnz, dtype=dC.dtype, device=dev)
-    step = max(1, (1 << 26) // max(dC2.shape[1], 1))
-    for s0 in range(0, A.nnz, step):
-        sl = slice(s0, s0 + step)
-        out[sl] = (dC2[rows[sl]] * B2[cols[sl]]).sum(dim=1)
-    return (alpha * out).to(A.values.device)
+    """d values[j] = alpha * <dC[row_j], B[col_j]> (the product's adjoint projected
+    on A's pattern), one ``trnsparse_csr_sddmm`` launch over the stored entries."""
+    dev = dC.device if dC.is_cuda else _dev_of(B)
+    lay = A.device_layout(dev)
+    G = _on(dC.reshape(dC.shape[0], -1), dev, A.dtype)
+    X = _on(B.reshape(B.shape[0], -1), dev, A.dtype)
+    k = G.shape[1]
+    out = torch.empty(A.nnz, dtype=A.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_csr_sddmm", A.shape[0], A.shape[1], k, A.nnz, _lib.index_code(lay["row_ptrs"].dtype),
+                  _lib.dtype_code(A.dtype), lay["row_ptrs"].data_ptr(), lay["col_indices"].data_ptr(), G.data_ptr(),
+                  k, X.data_ptr(), k, float(alpha), out.data_ptr(), _lib.stream_handle(dev))
+    return out.to(A.values.device)
 
 
 class _CsrProductFn(torch.autograd.Function):
@@ -432,8 +463,8 @@ class _CsrProductFn(torch.autograd.Function):
         (X,) = ctx.saved_tensors
         dvals = dX = dY = None
         if ctx.needs_input_grad[1]:
-            AT, _ = _csr_transpose(A)
             g = dout.to(X.device).contiguous()
+            AT = _csr_transpose(A, g.device if g.is_cuda else _dev_of(g))
             dX = _spmv_impl(AT, g, alpha, None, 0.0) if X.dim() == 1 else _spmm_impl(AT, g, alpha, None, 0.0)
         if ctx.needs_input_grad[2]:
             dY = beta * dout
@@ -442,27 +473,35 @@ class _CsrProductFn(torch.autograd.Function):
         return dvals, dX, dY, None, None, None
 
 
-def _bsr_transpose(A: BSRMatrix) -> BSRMatrix:
-    """A^T as a BSRMatrix: transposed blocks in the transposed pattern's order (cached)."""
+def _bsr_transpose(A: BSRMatrix, dev: torch.device) -> BSRMatrix:
+    """A^T as a BSRMatrix on ``dev``: the transposed block pattern built on
+    the device (``trnsparse_csr_transpose`` over the block pointers) and the
+    blocks gathered and transposed by ``trnsparse_bsr_blocks_transpose``. One
+    cache slot per matrix, keyed by the fingerprint of A's blocks and indices
+    and replaced when they change (so repeated in-place updates of A.blocks
+    never accumulate copies)."""
     from .formats import _fingerprint
 
-    key = ("transpose", _fingerprint(A.blocks, A.block_col_indices, A.block_row_ptrs))
+    key = ("bsr_transpose", str(dev))
+    fp = _fingerprint(A.blocks, A.block_col_indices, A.block_row_ptrs)
     hit = A._dev.get(key)
-    if hit is not None:
-        return hit
+    if hit is not None and hit[0] == fp:
+        return hit[1]
+    A._dev.pop(key, None)  # free the old transpose before building the new one
     b = A.block_size
-    rp = A.block_row_ptrs.to(torch.long).cpu()
-    ci = A.block_col_indices.to(torch.long).cpu()
-    R = rp.numel() - 1
+    lay = A.device_layout(dev)
+    R = lay["row_ptr"].numel() - 1
     Cn = -(-A.shape[1] // b)
-    rows = torch.repeat_interleave(torch.arange(R), rp[1:] - rp[:-1])
-    order = torch.argsort(ci * max(R, 1) + rows, stable=True)
-    rpt = torch.zeros(Cn + 1, dtype=torch.long)
-    rpt[1:] = torch.cumsum(torch.bincount(ci, minlength=Cn)[:Cn], 0)
-    blocks_t = A.blocks.detach()[order.to(A.blocks.device)].transpose(1, 2).contiguous()
-    AT = BSRMatrix(blocks=blocks_t, block_col_indices=rows[order], block_row_ptrs=rpt, shape=(A.shape[1], A.shape[0]),
+    rpt, colt, perm, _ = _transpose_structure(lay["row_ptr"], lay["col_idx"], R, Cn, False, A._dev, dev)
+    blocks = lay["blocks"]
+    bt = torch.empty_like(blocks)
+    if A.n_blocks:
+        with torch.cuda.device(dev):
+            _lib.call("trnsparse_bsr_blocks_transpose", A.n_blocks, b, blocks.element_size(), blocks.data_ptr(),
+                      perm.data_ptr(), bt.data_ptr(), _lib.stream_handle(dev))
+    AT = BSRMatrix(blocks=bt, block_col_indices=colt, block_row_ptrs=rpt, shape=(A.shape[1], A.shape[0]),
                    block_size=b)
-    A._dev[key] = AT
+    A._dev[key] = (fp, AT)
     return AT
 
 
@@ -498,7 +537,9 @@ class _BsrSpmmFn(torch.autograd.Function):
         (B,) = ctx.saved_tensors
         dblocks = dB = None
         if ctx.needs_input_grad[1]:
-            dB = _bsr_spmm_impl(_bsr_transpose(A), dC.to(device=B.device).contiguous()).to(B.dtype)
+            g = dC.contiguous()
+            dB = _bsr_spmm_impl(_bsr_transpose(A, g.device if g.is_cuda else _dev_of(g)), g).to(B.dtype)
+            dB = dB.to(B.device)
         if ctx.needs_input_grad[0]:
             dblocks = _bsr_blocks_grad(A, dC, B)
         return dblocks, dB, None
