@@ -277,7 +277,7 @@ def run_ours(args, ws, rank, local):
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_spmv(A, x_host)
     if rank == 0 and ws == 1 and not args.no_extra:
-        line["extra"] = run_extras(pk, flush)
+        line["extra"] = run_extras(pk, flush, reps=args.reps)
     if ws > 1 and not args.no_extra:
         sharded = run_sharded_cg(ws, rank, local, pk)
         if rank == 0:
@@ -420,83 +420,141 @@ def time_call(f, reps: int, flush: L2Flush | None) -> float:
     return out[len(out) // 2]
 
 
-def run_extras(pk: dict, flush: L2Flush) -> dict:
-    """Secondary rows: the other benchmark configurations, one call each.
+def graph_k(f, k: int) -> float:
+    """Milliseconds per call of ``f`` over ``k`` back-to-back calls captured in
+    one CUDA graph (launch overhead amortised; inputs that fit in L2 stay warm)."""
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        f()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(k):
+                f()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / k
 
-    bsr_spmm / screened_spmm: nonzero-block FLOP/s (2*128*128*k per stored
-    block; fp32 runs 3xTF32, i.e. three tensor-core passes per FLOP counted).
-    Peaks: bf16 = measured cuBLAS burst; tf32 = bf16 x 0.5 (the B200 spec
-    ratio of dense TF32 to BF16), so fp32 3xTF32 tops out near 1/6 of bf16.
-    """
+
+def row_bsr_spmm(pk: dict, flush: L2Flush, reps: int, cases: tuple = ("config1", "grid128"),
+                 dtypes: tuple = ("f32", "bf16")) -> dict:
+    """Config 1 and a scaled variant (128 x 128 block grid, k = 512, same
+    distribution), fp32 (3xTF32) and bf16. Nonzero-block FLOPs
+    2*128*128*k per stored block. ``ms`` = one call replayed from a graph
+    after an L2 flush (cold); ``ms_back_to_back`` = K calls in one graph / K
+    (the launch latency amortised; config 1's 7.5 MB of inputs stay in L2)."""
     import trnsparse_b200 as ts
     from trnsparse_b200 import workloads as w
 
     tf32 = 0.5 * pk["bf16_tflops"]
     ex = {}
-    # config 1 and a scaled variant with the same distribution
     for name, grid, k in [("config1_bsr_spmm", 16, 256), ("bsr_spmm_grid128_k512", 128, 512)]:
+        if name.split("_")[0] not in cases and name.split("_")[2] not in cases:
+            continue
         for dt, tag in [(torch.float32, "f32_3xtf32"), (torch.bfloat16, "bf16")]:
+            if tag.split("_")[0] not in dtypes:
+                continue
             A, B = w.bsr_random_grid(grid=grid, k=k, dtype=dt)
             Bd = B.cuda()
             small = grid == 16
-            ms = time_call(lambda: ts.bsr_spmm(A, Bd), 20, flush if small else None)
-            tfl = 2 * 128 * 128 * k * A.n_blocks / (ms * 1e-3) / 1e12
+            f = lambda: ts.bsr_spmm(A, Bd)  # noqa: E731
+            ms = time_call(f, reps, flush if small else None)
+            ms_k = graph_k(f, 20 if small else 5)
+            flop = 2 * 128 * 128 * k * A.n_blocks
+            tfl = flop / (ms * 1e-3) / 1e12
+            tfl_k = flop / (ms_k * 1e-3) / 1e12
             peak = pk["bf16_tflops"] if dt == torch.bfloat16 else tf32 / 3
-            ex[f"{name}_{tag}"] = {"TFLOP/s": round(tfl, 1), "ms": round(ms, 4), "n_blocks": A.n_blocks,
-                                   "frac_of_peak": round(tfl / peak, 3),
-                                   "peak": ("bf16 measured" if dt == torch.bfloat16 else "tf32 derived / 3 passes"),
-                                   "l2": "flushed" if small else "inputs exceed L2",
-                                   "includes": ("B split/transpose (fp32) or none (bf16), C clearing when a block-row is split, "
-                                                "tensor-core kernel")}
+            ex[f"{name}_{tag}"] = {
+                "TFLOP/s": round(tfl, 1), "ms": round(ms, 4), "ms_back_to_back": round(ms_k, 4),
+                "n_blocks": A.n_blocks, "frac_of_peak": round(tfl / peak, 3),
+                "roofline": {"bound": "tensor", "achieved": round(tfl_k, 1), "peak": round(peak, 1),
+                             "unit": "TFLOP/s", "frac": round(tfl_k / peak, 3),
+                             "peak_source": ("bf16 measured (burst)" if dt == torch.bfloat16 else
+                                             "tf32 = 0.5 x measured bf16, / 3 passes"),
+                             "time": "back to back"},
+                "l2": "flushed before the single call" if small else "inputs exceed L2",
+                "includes": "every kernel of the call (B split for fp32, C clearing when a block-row is split)"}
             del A, B, Bd
-    # config 2b: CSR spmm, k = 32
+    return ex
+
+
+def row_csr_spmm(pk: dict, flush: L2Flush, reps: int) -> dict:
+    """Config 2b: CSR spmm, k = 32 (inputs exceed L2)."""
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+
     A = w.poisson2d_csr(2048)
     Bm = w.poisson_rhs(A.shape[0], 32).cuda()
     n = A.shape[0]
-    ms = time_call(lambda: ts.spmm(A, Bm), 10, None)
+    ms = time_call(lambda: ts.spmm(A, Bm), reps, None)
     nb = 8 * A.nnz + 4 * (n + 1) + 4 * n * 32 * 2
-    ex["config2b_csr_spmm_k32"] = {"GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
-                                   "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
-    del Bm
-    # config 3: screened_spmm with 2-D pair bounds
+    return {"config2b_csr_spmm_k32": {"GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
+                                      "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}}
+
+
+def row_screened(pk: dict, flush: L2Flush, reps: int) -> dict:
+    """Config 3: screened_spmm with 2-D pair bounds."""
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+
+    tf32 = 0.5 * pk["bf16_tflops"]
     Af, Qf, Bf, _, thr = w.fock_like()
     Ad, Qd, Bd = Af.cuda(), Qf.cuda(), Bf.cuda()
     del Af, Qf, Bf
-    ms = time_call(lambda: ts.screened_spmm(Ad, Qd, Bd, thr), 10, None)
+    ms = time_call(lambda: ts.screened_spmm(Ad, Qd, Bd, thr), reps, None)
     fl = 2 * 8192 * 8192 * 512  # every 128x128 block has a surviving pair (unsorted centres)
-    ex["config3_screened_spmm"] = {"TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4),
-                                   "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / (tf32 / 3), 3),
-                                   "peak": "tf32 derived / 3 passes"}
-    del Ad, Qd, Bd
-    # config 4: block-sparse attention, 16 heads x 16384 x 128 bf16, sliding window 8 + 2 global
+    return {"config3_screened_spmm": {"TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4),
+                                      "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / (tf32 / 3), 3),
+                                      "peak": "tf32 derived / 3 passes"}}
+
+
+def row_attention(pk: dict, flush: L2Flush, reps: int) -> dict:
+    """Config 4: block-sparse attention forward and backward (bf16)."""
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+    from trnsparse_b200.ops import _attn_backward, _attn_forward
+
+    ex = {}
     mask = w.sliding_window_mask()
     Qa, Ka, Va = (t.cuda() for t in w.attention_inputs())
-    ms = time_call(lambda: ts.block_sparse_attention_tiled(Qa, Ka, Va, mask), 5, None)
+    ms = time_call(lambda: ts.block_sparse_attention_tiled(Qa, Ka, Va, mask), max(3, reps // 2), None)
     fl = 4 * 128 ** 3 * mask.n_blocks * 16
     ex["config4_block_sparse_attention_bf16"] = {
         "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "blocks_per_head": mask.n_blocks,
         "frac_of_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 3), "peak": "bf16 measured",
         "note": "FLOPs counted once per block (QK^T + PV); one pass with an online softmax"}
-    # config 4 backward: dQ, dK, dV on the tensor cores, with the
-    # forward's saved log-sum-exp (as autograd runs it)
-    from trnsparse_b200.ops import _attn_backward, _attn_forward
-
+    # backward: dQ, dK, dV on the tensor cores, with the forward's saved log-sum-exp (as autograd runs it)
     Oa, lse = _attn_forward(Qa, Ka, Va, mask, 128 ** -0.5, want_lse=True)
     dOa = torch.randn(Oa.shape, generator=torch.Generator().manual_seed(5)).to(Oa.dtype).cuda()
-    ms = time_call(lambda: _attn_backward(Qa, Ka, Va, Oa, dOa, mask, 128 ** -0.5, lse=lse), 3, None)
+    ms = time_call(lambda: _attn_backward(Qa, Ka, Va, Oa, dOa, mask, 128 ** -0.5, lse=lse), max(3, reps // 3), None)
     flb = 10 * 128 ** 3 * mask.n_blocks * 16
     ex["config4_attention_backward_bf16"] = {
         "TFLOP/s": round(flb / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 3),
         "frac_of_peak": round(flb / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 3), "peak": "bf16 measured",
         "note": "tcgen05 kernels (dQ row-first, dK/dV column-first); FLOPs = S, dP, dQ, dK, dV per block "
-                "(10*128^3), S and dP are computed in both passes"}
-    del Qa, Ka, Va, Oa, dOa
-    # config 5: Jacobi-PCG, 200 iterations, tol 0
+                "(10*128^3)"}
+    return ex
+
+
+def row_cg(pk: dict, flush: L2Flush, reps: int) -> dict:
+    """Config 5: Jacobi-PCG, tol 0, max_iter 200, and the config-5 BSR SpMV."""
+    import trnsparse_b200 as ts
+    from trnsparse_b200 import workloads as w
+    from trnsparse_b200.iterative import _cg_bsr_device
+
+    ex = {}
     A5, b5 = w.block_pentadiagonal_spd()
     M5 = ts.jacobi_preconditioner_bsr(A5)
     bd = b5.cuda()
-    from trnsparse_b200.iterative import _cg_bsr_device
-
     _cg_bsr_device(A5, bd, None, 0.0, 5, M5)
     torch.cuda.synchronize()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -512,12 +570,35 @@ def run_extras(pk: dict, flush: L2Flush) -> dict:
                 "(iters_reported stays max_iter, as the reference returns); the whole solve is one cooperative "
                 "launch that returns at the break, so ms_total covers the executed iterations only"}
     xv = bd.unsqueeze(1)
-    ms = time_call(lambda: ts.bsr_spmm(A5, xv), 10, None)
+    ms = time_call(lambda: ts.bsr_spmm(A5, xv), reps, None)
     nb = A5.n_blocks * 128 * 128 * 4 + 4 * A5.n_blocks + 4 * 2049 + 8 * A5.shape[0]
     ex["config5_bsr_spmv"] = {"GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4),
                               "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
-    del A5, M5, bd, xv
-    ex.update(run_format_extras(pk))
+    return ex
+
+
+def row_formats(pk: dict, flush: L2Flush, reps: int) -> dict:
+    return run_format_extras(pk)
+
+
+ROWS = {"bsr_spmm": row_bsr_spmm,
+        # single bsr_spmm cases, for profiling one kernel configuration
+        "bsr_spmm_config1_f32": lambda pk, fl, r: row_bsr_spmm(pk, fl, r, ("config1",), ("f32",)),
+        "bsr_spmm_config1_bf16": lambda pk, fl, r: row_bsr_spmm(pk, fl, r, ("config1",), ("bf16",)),
+        "bsr_spmm_grid128_f32": lambda pk, fl, r: row_bsr_spmm(pk, fl, r, ("grid128",), ("f32",)),
+        "bsr_spmm_grid128_bf16": lambda pk, fl, r: row_bsr_spmm(pk, fl, r, ("grid128",), ("bf16",)), "csr_spmm": row_csr_spmm, "screened": row_screened,
+        "attention": row_attention, "cg": row_cg, "formats": row_formats}
+
+
+DEFAULT_ROWS = ("bsr_spmm", "csr_spmm", "screened", "attention", "cg", "formats")
+
+
+def run_extras(pk: dict, flush: L2Flush, only: list[str] | None = None, reps: int = 10) -> dict:
+    """Secondary rows: the other benchmark configurations (``only`` selects row groups)."""
+    ex = {}
+    for name, fn in ROWS.items():
+        if (only is None and name in DEFAULT_ROWS) or (only is not None and name in only):
+            ex.update(fn(pk, flush, reps))
     return ex
 
 
@@ -642,6 +723,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary configurations")
+    ap.add_argument("--only", default=None,
+                    help="comma-separated row groups (" + ",".join(ROWS) + "): run only these secondary rows, "
+                         "no headline (for profiling)")
+    ap.add_argument("--reps", type=int, default=10, help="timed calls per secondary row")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -652,6 +737,12 @@ def main():
             print(json.dumps(line), flush=True)
         return
     ws, rank, local = dist_setup()
+    if args.only:
+        line = {"only": args.only.split(","),
+                "extra": run_extras(peaks(), L2Flush(), args.only.split(","), args.reps)}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     line = run_ours(args, ws, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
