@@ -237,13 +237,17 @@ TRNSPARSE_API int trnsparse_bsr_split_tf32(int64_t count, const float* src, floa
  * tensor-core kernel (3xTF32, fp32 in/out): the reference's screened_spmm
  * (trnsparse/ops.py:213-277; nki_screened_spmm, trnsparse/nki/dispatch.py:
  * 487-494, kernels.py:86-155). A is M x K (row stride lda), B is K x N
- * (ldb), C is M x N (ldc), all row-major fp32; lda, ldq multiples of 4.
+ * (ldb), C is M x N (ldc), all row-major fp32; lda, ldq, ldc multiples of 4
+ * and C 16-byte aligned (C is written by TMA stores).
  *   bounds_kind 1: `bounds` is the length-M diag_integrals vector (M == K);
  *                  mask[i,j] = sqrt|d_i| * sqrt|d_j| > fp32(sqrt(threshold)).
  *   bounds_kind 2: `bounds` is the M x K pair-bound matrix Q (row stride ldq)
  *                  of screening.py's schwarz_bounds; mask = Q > fp32(sqrt(thr))
  *                  (screen_quartets, screening.py:29-40).
- * K chunks with no surviving pair issue no MMA. Workspace:
+ * K chunks with no surviving pair issue no MMA. One persistent CTA per SM
+ * takes an equal share of the (128-row x N-tile output tile, 128-wide K
+ * block) pairs; tiles shared by two CTAs are reduce-added into a cleared C.
+ * Workspace:
  * trnsparse_screened_spmm_workspace_size(K, N) bytes (B^T split). */
 TRNSPARSE_API size_t trnsparse_screened_spmm_workspace_size(int64_t K, int64_t N);
 TRNSPARSE_API int trnsparse_screened_spmm(int64_t M, int64_t K, int64_t N, const float* A, int64_t lda,
@@ -492,6 +496,30 @@ TRNSPARSE_API int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const 
 TRNSPARSE_API int trnsparse_csr_sddmm(int64_t m, int64_t n, int64_t k, int64_t nnz, int index_type, int dtype,
                         const void* row_ptrs, const void* col_indices, const void* G, int64_t ldg,
                         const void* X, int64_t ldx, double alpha, void* out, void* stream);
+
+/* ---- block gradients on the tensor cores ------------------------------
+ * 128 x 128 output tiles of X Y^T, X (mx x K, row stride ldx) and Y
+ * (my x K, ldy) row-major, dtype F32 (3xTF32) or BF16 (fp32 accumulation):
+ *   tiles != NULL: packed. tiles holds n_tiles (i, j) int32 pairs (device);
+ *     tile u = X[128 i : 128 i + 128] . Y[128 j : 128 j + 128]^T goes to rows
+ *     [128 u, 128 u + 128) of `out` (128 columns, row stride ldo): the BSR
+ *     block gradient dblocks[k] = dC_i B_j^T of the reference's
+ *     _BSRSpMMFunction.backward (trnsparse/nki/dispatch.py:331-369).
+ *   tiles == NULL: dense. out (out_rows x out_cols <= mx x my, ldo) = X Y^T,
+ *     optionally masked: mask_kind 1, bounds = diagonal integrals d (square):
+ *     keep fl(sqrt|d_r| sqrt|d_c|) > fp32(sqrt(threshold)); mask_kind 2,
+ *     bounds = pair-bound matrix Q (row stride ldq): keep Q[r, c] >
+ *     fp32(sqrt(threshold)). The screened dA = (dC B^T) o mask of
+ *     _ScreenedSpMMFunction.backward (nki/dispatch.py:447-484).
+ * out: F32 or BF16, 16-byte aligned rows. Rows/columns past X's or Y's edge
+ * read as zero. Workspace: trnsparse_nt_tc_workspace_size(mx, my, K, dtype)
+ * bytes (F32: the tf32 hi/lo split of X and Y; BF16: padded copies, used
+ * only when an operand's rows are not 16-byte aligned or K < 64). */
+TRNSPARSE_API size_t trnsparse_nt_tc_workspace_size(int64_t mx, int64_t my, int64_t K, int dtype);
+TRNSPARSE_API int trnsparse_nt_tc(int64_t mx, int64_t my, int64_t K, int dtype, const void* X, int64_t ldx,
+                    const void* Y, int64_t ldy, const int* tiles, int64_t n_tiles, void* out, int64_t ldo,
+                    int out_dtype, int64_t out_rows, int64_t out_cols, int mask_kind, const float* bounds,
+                    int64_t ldq, double threshold, void* ws, size_t ws_bytes, void* stream);
 
 /* ---- transposes (autograd adjoints and spmv_symmetric) ----------------
  * Transposed structure of a CSR matrix on the device: the reference builds

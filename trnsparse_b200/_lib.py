@@ -100,6 +100,9 @@ SIGNATURES.update({
     "trnsparse_csr_transpose_workspace_size": [_i64, _i64, _i64],
     "trnsparse_csr_transpose": [_i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _p, _p, _sz, _p],
     "trnsparse_csr_sddmm": [_i64, _i64, _i64, _i64, _i32, _i32, _p, _p, _p, _i64, _p, _i64, _f64, _p, _p],
+    "trnsparse_nt_tc_workspace_size": [_i64, _i64, _i64, _i32],
+    "trnsparse_nt_tc": [_i64, _i64, _i64, _i32, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i32, _i64, _i64, _i32, _p,
+                        _i64, _f64, _p, _sz, _p],
     "trnsparse_gather": [_i64, _i32, _p, _p, _p, _p],
     "trnsparse_bsr_blocks_transpose": [_i64, _i32, _i32, _p, _p, _p, _p],
 })
@@ -115,6 +118,7 @@ _RESTYPE = {
     "trnsparse_csr_from_dense_workspace_size": C.c_size_t,
     "trnsparse_coo_to_csr_workspace_size": C.c_size_t,
     "trnsparse_csr_transpose_workspace_size": C.c_size_t,
+    "trnsparse_nt_tc_workspace_size": C.c_size_t,
     "trnsparse_bsr_spmm_tc_plan_capacity": C.c_int64,
     "trnsparse_screened_spmm_workspace_size": C.c_size_t,
     "trnsparse_peer_comm_bytes": C.c_size_t,

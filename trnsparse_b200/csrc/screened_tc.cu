@@ -21,253 +21,305 @@
 namespace tsb {
 namespace {
 
-constexpr int kScThreads = 256;  // warps 0-3: TMA / MMA / TMEM drain; warps 4-7: mask transform
+constexpr int kScThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue, warps 6-9 mask transform
+constexpr int kScSmemMax = 232448;
 
 template <int BN>
 struct ScLayout {
-  static constexpr int kATile = 128 * 128;
-  static constexpr int kBTile = BN * 128;
+  static constexpr int kATile = 128 * 128;  // 128 rows x 32 fp32: A (then its tf32 hi), or Q (then A's lo)
+  static constexpr int kBTile = BN * 128;   // BN rows of B^T x 32 fp32, hi and lo
   static constexpr int kStage = 2 * (kATile + kBTile);
-  static constexpr int kStages = 200 * 1024 / kStage;
-  static constexpr int kSmem = kStages * kStage + 1024;
-  static_assert(kStages * kStage >= 128 * (BN + 4) * 4, "epilogue tile must fit in the operand ring");
+  static constexpr int kEpi = 4 * 2 * 4096;  // per epilogue warp: two 32 x 32 fp32 staging tiles
+  static constexpr int kBarBytes = 1024;
+  static constexpr int kAlign = 1024;        // slack to align the window to 1024 bytes
+  static constexpr int kStages = (kScSmemMax - kAlign - kEpi - kBarBytes) / kStage;
+  static constexpr int kEpiOff = kStages * kStage;
+  static constexpr int kBarOff = kEpiOff + kEpi;
+  static constexpr int kSmem = kBarOff + kBarBytes + kAlign;
+  static_assert(kStages >= 2 && kStages <= 4, "operand ring");
 };
+
+struct ScBars {
+  uint64_t full[4], xf[4], empty[4], acc_full[2], acc_empty[2];
+  uint32_t tmem_slot;
+  int abort_flag;
+  int survive[4][4];
+  int have[2];
+};
+
+// The CTA's share of the work: the linear range [lo, hi) of (output tile, K block) pairs,
+// output tile = row_tile * nt + n_tile, K block fastest. Consecutive pairs of one output tile
+// form a segment; a segment that does not cover its tile's whole K range adds into C.
+struct ScSeg {
+  int row_tile, n_tile, kb0, kb1;
+  bool partial;
+};
+struct ScWalk {
+  int64_t pos, hi;
+  int nkb, nt;
+  __device__ bool next(ScSeg& g) {
+    if (pos >= hi) return false;
+    const int64_t tile = pos / nkb;
+    const int64_t end = min(hi, (tile + 1) * nkb);
+    g.row_tile = static_cast<int>(tile / nt);
+    g.n_tile = static_cast<int>(tile % nt);
+    g.kb0 = static_cast<int>(pos - tile * nkb);
+    g.kb1 = static_cast<int>(end - tile * nkb);
+    g.partial = g.kb0 > 0 || g.kb1 < nkb;
+    pos = end;
+    return true;
+  }
+};
+__device__ __forceinline__ ScWalk sc_walk(int64_t W, int nkb, int nt) {
+  const int64_t G = gridDim.x;
+  return ScWalk{W * blockIdx.x / G, W * (blockIdx.x + 1) / G, nkb, nt};
+}
 
 // mode 1: q_vec (length K == M) holds diag integrals, mask = fl(Qi*Qj) > t
 // mode 2: tq maps the 2-D bound matrix Q (M x K), mask = Q > t
+// Persistent: gridDim.x CTAs split the (output tile, K block) space evenly (sc_walk).
 template <int BN>
 __global__ void __launch_bounds__(kScThreads, 1)
 screened_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tq,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
-                   const float* __restrict__ q_vec, int mode, float t, int64_t M, int64_t K, int64_t N, int nkb,
-                   int nsplit, float* __restrict__ C, int64_t ldc) {
+                   const __grid_constant__ CUtensorMap tc, const float* __restrict__ q_vec, int mode, float t,
+                   int64_t M, int64_t K, int64_t N, int nkb, int nt) {
   using Lay = ScLayout<BN>;
   constexpr int S = Lay::kStages;
   extern __shared__ __align__(16) uint8_t dsmem_sc[];
-  __shared__ __align__(8) uint64_t full_bar[S];
-  __shared__ __align__(8) uint64_t xf_bar[S];
-  __shared__ __align__(8) uint64_t empty_bar[S];
-  __shared__ __align__(8) uint64_t done_bar;
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-  __shared__ int survive[S][4];
-  __shared__ int any_mma;
-  __shared__ float qrow[128];
-
   const uint32_t raw = smem_u32(dsmem_sc);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t* const sbase = dsmem_sc + (base - raw);
+  uint8_t* const sbase = dsmem_sc + (((raw + 1023u) & ~1023u) - raw);
+  ScBars& Bs = *reinterpret_cast<ScBars*>(sbase + Lay::kBarOff);
   auto a_hi = [&](int s) { return sbase + s * Lay::kStage; };
   auto a_lo = [&](int s) { return sbase + s * Lay::kStage + Lay::kATile; };
   auto b_hi = [&](int s) { return sbase + s * Lay::kStage + 2 * Lay::kATile; };
   auto b_lo = [&](int s) { return sbase + s * Lay::kStage + 2 * Lay::kATile + Lay::kBTile; };
-
-  const int warp = threadIdx.x >> 5;
-  const int row_tile = blockIdx.x / nsplit;
-  const int part = blockIdx.x - row_tile * nsplit;
-  const int kb0 = static_cast<int>((static_cast<int64_t>(nkb) * part) / nsplit);
-  const int kb1 = static_cast<int>((static_cast<int64_t>(nkb) * (part + 1)) / nsplit);
-  const int total = (kb1 - kb0) * 4;  // 32-wide fp32 chunks
-  const int n0 = blockIdx.y * BN;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t W = static_cast<int64_t>((M + 127) / 128) * nt * nkb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&xf_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&Bs.full[s], 1);
+      mbar_init(&Bs.xf[s], 1);
+      mbar_init(&Bs.empty[s], 1);
     }
-    mbar_init(&done_bar, 1);
-    abort_flag = (base & 1023u) ? 1 : 0;
-    if (abort_flag) record_device_error(DEVERR_SELFCHECK_SMEM);
-    any_mma = 0;
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&Bs.acc_full[i], 1);
+      mbar_init(&Bs.acc_empty[i], 128);
+    }
+    Bs.abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb_hi);
     tma_prefetch_desc(&tb_lo);
+    tma_prefetch_desc(&tc);
     if (mode == 2) tma_prefetch_desc(&tq);
   }
-  if (mode == 1 && threadIdx.x >= 128) {
-    const int64_t r = static_cast<int64_t>(row_tile) * 128 + (threadIdx.x - 128);
-    qrow[threadIdx.x - 128] = r < M ? __fsqrt_rn(fabsf(q_vec[r])) : 0.f;
-  }
   if (warp == 1) {
-    tmem_alloc(&tmem_slot, BN);
+    tmem_alloc(&Bs.tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_slot;
+  const uint32_t tmem = Bs.tmem_slot;
+  volatile int* abort_flag = &Bs.abort_flag;
 
-  if (warp == 0 && elect_lane0()) {
+  if (warp == 0) {
     // ---------------- TMA producer
-    int issued = 0;
-    for (int it = 0; it < total; ++it) {
-      const int s = it % S, use = it / S;
-      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1)) {
-        atomicExch(&abort_flag, 1);
-        break;
+    if (lane == 0) {
+      ScWalk wk = sc_walk(W, nkb, nt);
+      ScSeg g;
+      int it = 0;
+      bool ok = true;
+      while (ok && wk.next(g)) {
+        const int n0 = g.n_tile * BN;
+        for (int kc = g.kb0 * 4; ok && kc < g.kb1 * 4; ++kc, ++it) {
+          const int s = it % S, use = it / S;
+          if (use > 0 && !mbar_wait(&Bs.empty[s], (use - 1) & 1)) { ok = false; break; }
+          if (*abort_flag) { ok = false; break; }
+          const int kx = kc * 32;  // K coordinate of the 32-wide chunk
+          mbar_arrive_expect_tx(&Bs.full[s], mode == 2 ? Lay::kStage : Lay::kStage - Lay::kATile);
+          tma_load_2d(a_hi(s), &ta, kx, g.row_tile * 128, &Bs.full[s]);
+          if (mode == 2) tma_load_2d(a_lo(s), &tq, kx, g.row_tile * 128, &Bs.full[s]);
+          tma_load_2d(b_hi(s), &tb_hi, kx, n0, &Bs.full[s]);
+          tma_load_2d(b_lo(s), &tb_lo, kx, n0, &Bs.full[s]);
+        }
       }
-      if (*(volatile int*)&abort_flag) break;
-      const int kx = (kb0 + it / 4) * 128 + (it % 4) * 32;  // K coordinate of the chunk
-      mbar_arrive_expect_tx(&full_bar[s], mode == 2 ? Lay::kStage : Lay::kStage - Lay::kATile);
-      tma_load_2d(a_hi(s), &ta, kx, row_tile * 128, &full_bar[s]);
-      if (mode == 2) tma_load_2d(a_lo(s), &tq, kx, row_tile * 128, &full_bar[s]);
-      tma_load_2d(b_hi(s), &tb_hi, kx, n0, &full_bar[s]);
-      tma_load_2d(b_lo(s), &tb_lo, kx, n0, &full_bar[s]);
-      issued = it + 1;
+      if (!ok) {
+        atomicExch(&Bs.abort_flag, 1);
+        // never leave the CTA with copies in flight: wait for the fills nobody consumed
+        for (int i = (it > S ? it - S : 0); i < it; ++i) mbar_wait(&Bs.full[i % S], (i / S) & 1);
+      }
     }
-    if (*(volatile int*)&abort_flag) {
-      for (int it = (issued > S ? issued - S : 0); it < issued; ++it) mbar_wait(&full_bar[it % S], (it / S) & 1);
-    }
-  } else if (warp == 1 && elect_lane0()) {
+  } else if (warp == 1) {
     // ---------------- MMA issuer
-    constexpr uint32_t idesc = make_idesc(MmaKind::TF32, 128, BN);
-    bool acc = false;
-    for (int it = 0; it < total; ++it) {
-      if (*(volatile int*)&abort_flag) break;
-      const int s = it % S, use = it / S;
-      if (!mbar_wait(&xf_bar[s], use & 1)) {
-        atomicExch(&abort_flag, 1);
-        break;
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(MmaKind::TF32, 128, BN);
+      ScWalk wk = sc_walk(W, nkb, nt);
+      ScSeg g;
+      int it = 0, q = 0;
+      bool ok = !*abort_flag;
+      while (ok && wk.next(g)) {
+        const int acc = q & 1;
+        if (q >= 2 && !mbar_wait(&Bs.acc_empty[acc], ((q >> 1) - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        bool started = false;
+        for (int kc = g.kb0 * 4; kc < g.kb1 * 4; ++kc, ++it) {
+          const int s = it % S, use = it / S;
+          if (*abort_flag || !mbar_wait(&Bs.xf[s], use & 1)) { ok = false; break; }
+          tc_fence_after();
+          if (Bs.survive[s][0] | Bs.survive[s][1] | Bs.survive[s][2] | Bs.survive[s][3]) {
+            const uint32_t ah = smem_u32(a_hi(s)), al = smem_u32(a_lo(s));
+            const uint32_t bh = smem_u32(b_hi(s)), bl = smem_u32(b_lo(s));
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint32_t off = ks * 32;
+              umma<MmaKind::TF32>(d, smem_desc_sw128(ah + off), smem_desc_sw128(bh + off), idesc, started);
+              started = true;
+              umma<MmaKind::TF32>(d, smem_desc_sw128(ah + off), smem_desc_sw128(bl + off), idesc, true);
+              umma<MmaKind::TF32>(d, smem_desc_sw128(al + off), smem_desc_sw128(bh + off), idesc, true);
+            }
+          }
+          umma_commit(&Bs.empty[s]);
+        }
+        if (!ok) break;
+        Bs.have[acc] = started ? 1 : 0;
+        __threadfence_block();
+        umma_commit(&Bs.acc_full[acc]);
+        ++q;
       }
+      if (!ok) atomicExch(&Bs.abort_flag, 1);
+    }
+  } else if (warp >= 6) {
+    // ---------------- mask + tf32 split of the A tile, in place (a thread per tile row)
+    const int tr = threadIdx.x - 192;
+    const int w4 = warp - 6;
+    ScWalk wk = sc_walk(W, nkb, nt);
+    ScSeg g;
+    int it = 0;
+    bool ok = !*abort_flag;
+    while (ok && wk.next(g)) {
+      float qi = 0.f;
+      if (mode == 1) {
+        const int64_t r = static_cast<int64_t>(g.row_tile) * 128 + tr;
+        qi = r < M ? __fsqrt_rn(fabsf(q_vec[r])) : 0.f;
+      }
+      for (int kc = g.kb0 * 4; kc < g.kb1 * 4; ++kc, ++it) {
+        const int s = it % S, use = it / S;
+        if (*abort_flag || !mbar_wait(&Bs.full[s], use & 1)) { ok = false; break; }
+        const int kx = kc * 32;
+        float4* arow = reinterpret_cast<float4*>(a_hi(s) + tr * 128);
+        float4* lrow = reinterpret_cast<float4*>(a_lo(s) + tr * 128);
+        int keep = 0;
+#pragma unroll
+        for (int pp = 0; pp < 8; ++pp) {
+          const int p = (pp + tr) & 7;   // rotate so 8 neighbouring rows hit 8 different banks
+          const int L = p ^ (tr & 7);    // logical 16-byte chunk held by physical chunk p
+          float4 a = arow[p];
+          float4 qv;
+          if (mode == 2) {
+            qv = lrow[p];
+          } else {
+            const int64_t c0 = kx + 4 * L;
+            float qc[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) qc[u] = (c0 + u < K) ? __fsqrt_rn(fabsf(__ldg(q_vec + c0 + u))) : 0.f;
+            qv = make_float4(__fmul_rn(qi, qc[0]), __fmul_rn(qi, qc[1]), __fmul_rn(qi, qc[2]), __fmul_rn(qi, qc[3]));
+          }
+          float v[4] = {qv.x > t ? a.x : 0.f, qv.y > t ? a.y : 0.f, qv.z > t ? a.z : 0.f, qv.w > t ? a.w : 0.f};
+          keep |= (qv.x > t) | (qv.y > t) | (qv.z > t) | (qv.w > t);
+          float h[4], l[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            h[u] = tf32_rna(v[u]);
+            l[u] = tf32_rna(v[u] - h[u]);
+          }
+          arow[p] = make_float4(h[0], h[1], h[2], h[3]);
+          lrow[p] = make_float4(l[0], l[1], l[2], l[3]);
+        }
+        const int wkeep = __any_sync(0xffffffffu, keep);
+        if (lane == 0) Bs.survive[s][w4] = wkeep;
+        fence_proxy_async_smem();  // generic-proxy writes -> tcgen05 (async proxy) reads
+        asm volatile("bar.sync 1, 128;\n" ::: "memory");
+        if (tr == 0) mbar_arrive(&Bs.xf[s]);
+      }
+    }
+    if (!ok) atomicExch(&Bs.abort_flag, 1);
+  } else {
+    // ---------------- epilogue warps 2-5: TMEM lane quadrant = warp % 4; 32 x 32 fp32 pieces
+    // staged (128-byte swizzle) and written by TMA: a store for a segment that covers its
+    // tile's whole K range, a reduce-add into the cleared C otherwise.
+    const int quad = warp & 3;
+    uint8_t* const stage0 = sbase + Lay::kEpiOff + (warp - 2) * 8192;
+    ScWalk wk = sc_walk(W, nkb, nt);
+    ScSeg g;
+    int q = 0, pc = 0;
+    bool ok = !*abort_flag;
+    while (wk.next(g)) {
+      const int acc = q & 1;
+      ok = ok && mbar_wait(&Bs.acc_full[acc], (q >> 1) & 1) && !*abort_flag;
       tc_fence_after();
-      if (survive[s][0] | survive[s][1] | survive[s][2] | survive[s][3]) {
-        const uint32_t ah = smem_u32(a_hi(s)), al = smem_u32(a_lo(s));
-        const uint32_t bh = smem_u32(b_hi(s)), bl = smem_u32(b_lo(s));
+      const bool have = __all_sync(0xffffffffu, ok) && *reinterpret_cast<volatile int*>(&Bs.have[acc]) != 0;
+      const int n0 = g.n_tile * BN;
+      const int64_t row0 = static_cast<int64_t>(g.row_tile) * 128 + quad * 32;
+      const uint32_t t_row = tmem + acc * BN + (static_cast<uint32_t>(quad * 32) << 16);
+      if (ok && (have || !g.partial)) {  // a screened-out partial segment adds nothing
+#pragma unroll 1
+        for (int p = 0; p < BN / 32 && n0 + p * 32 < N; ++p, ++pc) {
+          uint8_t* stage = stage0 + (pc & 1) * 4096;
+          if (pc >= 2) {
+            if (lane == 0) bulk_wait_read_1();  // the store issued two pieces ago has read its tile
+            __syncwarp();
+          }
+          uint32_t w[32];
+          if (have) {
+            tmem_ld32(t_row + p * 32, w);
+            tmem_wait_ld();
+          } else {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint32_t off = ks * 32;
-          umma<MmaKind::TF32>(tmem, smem_desc_sw128(ah + off), smem_desc_sw128(bh + off), idesc, acc);
-          acc = true;
-          umma<MmaKind::TF32>(tmem, smem_desc_sw128(ah + off), smem_desc_sw128(bl + off), idesc, true);
-          umma<MmaKind::TF32>(tmem, smem_desc_sw128(al + off), smem_desc_sw128(bh + off), idesc, true);
+            for (int i = 0; i < 32; ++i) w[i] = 0u;
+          }
+#pragma unroll
+          for (int x = 0; x < 8; ++x)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((x ^ (lane & 7)) * 16)) =
+                make_uint4(w[4 * x], w[4 * x + 1], w[4 * x + 2], w[4 * x + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < M) {
+            if (g.partial)
+              tma_reduce_add_2d(&tc, stage, n0 + p * 32, static_cast<int>(row0));
+            else
+              tma_store_2d(&tc, stage, n0 + p * 32, static_cast<int>(row0));
+            bulk_commit_group();
+          }
         }
       }
-      umma_commit(&empty_bar[s]);
+      tc_fence_before();
+      mbar_arrive(&Bs.acc_empty[acc]);
+      ++q;
     }
-    any_mma = acc ? 1 : 0;
-    umma_commit(&done_bar);
-  } else if (warp >= 4) {
-    // ---------------- mask + tf32 split, in place
-    const int tr = threadIdx.x - 128;  // tile row owned by this thread
-    const int w4 = warp - 4;
-    const float qi = mode == 1 ? qrow[tr] : 0.f;
-    for (int it = 0; it < total; ++it) {
-      if (*(volatile int*)&abort_flag) break;
-      const int s = it % S, use = it / S;
-      if (!mbar_wait(&full_bar[s], use & 1)) {
-        atomicExch(&abort_flag, 1);
-        break;
-      }
-      const int kx = (kb0 + it / 4) * 128 + (it % 4) * 32;
-      float4* arow = reinterpret_cast<float4*>(a_hi(s) + tr * 128);
-      float4* lrow = reinterpret_cast<float4*>(a_lo(s) + tr * 128);
-      int keep = 0;
-#pragma unroll
-      for (int pp = 0; pp < 8; ++pp) {
-        const int p = (pp + tr) & 7;   // rotate so 8 neighbouring rows hit 8 different banks
-        const int L = p ^ (tr & 7);    // logical 16-byte chunk held by physical chunk p
-        float4 a = arow[p];
-        float4 q;
-        if (mode == 2) {
-          q = lrow[p];
-        } else {
-          const int64_t c0 = kx + 4 * L;
-          float qc[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) qc[u] = (c0 + u < K) ? __fsqrt_rn(fabsf(__ldg(q_vec + c0 + u))) : 0.f;
-          q = make_float4(__fmul_rn(qi, qc[0]), __fmul_rn(qi, qc[1]), __fmul_rn(qi, qc[2]), __fmul_rn(qi, qc[3]));
-        }
-        float v[4] = {q.x > t ? a.x : 0.f, q.y > t ? a.y : 0.f, q.z > t ? a.z : 0.f, q.w > t ? a.w : 0.f};
-        keep |= (q.x > t) | (q.y > t) | (q.z > t) | (q.w > t);
-        float h[4], l[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          h[u] = tf32_rna(v[u]);
-          l[u] = tf32_rna(v[u] - h[u]);
-        }
-        arow[p] = make_float4(h[0], h[1], h[2], h[3]);
-        lrow[p] = make_float4(l[0], l[1], l[2], l[3]);
-      }
-      const int wkeep = __any_sync(0xffffffffu, keep);
-      if ((threadIdx.x & 31) == 0) survive[s][w4] = wkeep;
-      fence_proxy_async_smem();  // generic-proxy writes -> tcgen05 (async proxy) reads
-      asm volatile("bar.sync 1, 128;\n" ::: "memory");
-      if (threadIdx.x == 128) mbar_arrive(&xf_bar[s]);
-    }
+    if (lane == 0) bulk_wait_all();
   }
   __syncwarp();
-
-  // ---------------- epilogue
-  const bool ok = mbar_wait(&done_bar, 0);
-  tc_fence_after();
-  __syncthreads();
-  const bool single = nsplit == 1;  // this CTA owns the whole row tile: plain stores
-  const bool have = any_mma != 0;   // false: every chunk was screened out, the tile is zero
-  const bool run = ok && !*(volatile int*)&abort_flag && (have || single);
-  constexpr int LDS = BN + 4;
-  float* stile = reinterpret_cast<float*>(sbase);
-  if (run && have && warp < 4) {
-    const int r_local = warp * 32 + (threadIdx.x & 31);
-#pragma unroll 1
-    for (int cc = 0; cc < BN / 32; ++cc) {
-      uint32_t r[32];
-      tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + cc * 32, r);
-      tmem_wait_ld();
-      float4* dst = reinterpret_cast<float4*>(stile + r_local * LDS + cc * 32);
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                             __uint_as_float(r[4 * q + 3]));
-    }
-  }
-  __syncthreads();
-  if (run) {
-    const int64_t row0 = static_cast<int64_t>(row_tile) * 128;
-    const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (n0 + BN <= N);
-    if (vec) {
-      constexpr int F4 = BN / 4;
-      for (int f = threadIdx.x; f < 128 * F4; f += kScThreads) {
-        const int rl = f / F4, c4 = f - rl * F4;
-        const int64_t row = row0 + rl;
-        if (row < M) {
-          const float4 v = have ? *reinterpret_cast<const float4*>(stile + rl * LDS + 4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
-          float* dst = C + row * ldc + n0 + 4 * c4;
-          if (single) *reinterpret_cast<float4*>(dst) = v;
-          else red_add_v4(dst, __float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
-        }
-      }
-    } else {
-      for (int f = threadIdx.x; f < 128 * BN; f += kScThreads) {
-        const int rl = f / BN, c = f - rl * BN;
-        const int64_t row = row0 + rl, col = n0 + c;
-        if (row < M && col < N) {
-          if (single) C[row * ldc + col] = have ? stile[rl * LDS + c] : 0.f;
-          else red_add(C + row * ldc + col, __float_as_uint(stile[rl * LDS + c]));
-        }
-      }
-    }
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
 template <int BN>
 int launch_sc(const CUtensorMap& ta, const CUtensorMap& tq, const CUtensorMap& bhi, const CUtensorMap& blo,
-              const float* q_vec, int mode, float t, int64_t M, int64_t K, int64_t N, int nkb, int nsplit, float* C,
-              int64_t ldc, cudaStream_t st) {
+              const CUtensorMap& cm, const float* q_vec, int mode, float t, int64_t M, int64_t K, int64_t N,
+              int nkb, int nt, int grid, cudaStream_t st) {
   using Lay = ScLayout<BN>;
   auto kern = screened_tc_kernel<BN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kSmem);
   if (e != cudaSuccess) return cuda_status(e, "screened_tc: set smem");
-  const int64_t mt = (M + 127) / 128;
-  dim3 grid((unsigned)(mt * nsplit), (unsigned)((N + BN - 1) / BN));
-  kern<<<grid, kScThreads, Lay::kSmem, st>>>(ta, tq, bhi, blo, q_vec, mode, t, M, K, N, nkb, nsplit, C, ldc);
+  kern<<<grid, kScThreads, Lay::kSmem, st>>>(ta, tq, bhi, blo, cm, q_vec, mode, t, M, K, N, nkb, nt);
   TSB_CHECK_LAUNCH("screened_tc launch");
   return debug_sync(st, "screened_tc: main kernel (sync)");
 }
@@ -297,14 +349,20 @@ extern "C" int trnsparse_screened_spmm(int64_t M, int64_t K, int64_t N, const fl
   TSB_REQUIRE(ws && ws_bytes >= need, "screened_spmm: workspace too small (%zu < %zu)", ws_bytes, need);
   if (lda % 4 || (bounds_kind == 2 && ldq % 4))
     return fail(TRNSPARSE_ERR_ALIGN, "screened_spmm: row strides of A and Q must be multiples of 4 floats");
+  TSB_REQUIRE(ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0,
+              "screened_spmm: C must be 16-byte aligned with ldc a multiple of 4");
   cudaStream_t st = as_stream(stream);
   const int64_t nkb = (K + 127) / 128;
   const int64_t mt = (M + 127) / 128;
   const int bn = N > 128 ? 256 : 128;
   const int64_t nt = (N + bn - 1) / bn;
-  int nsplit = 1;
-  while (mt * nt * nsplit < sm_count() && nsplit * 2 <= nkb) nsplit *= 2;
-  if (nsplit > 1 || K == 0) {
+  TSB_REQUIRE(mt * nt * nkb < (1ll << 40) && nkb < (1 << 24), "screened_spmm: sizes out of range");
+  // persistent grid: the (output tile, K block) pairs split evenly over at most one CTA per SM
+  const int64_t W = mt * nt * nkb;
+  const int grid = static_cast<int>(W < sm_count() ? W : sm_count());
+  bool partial = false;  // does any CTA's range start or end inside an output tile?
+  for (int64_t c = 0; c <= grid && !partial && K > 0; ++c) partial = (W * c / grid) % nkb != 0;
+  if (partial || K == 0) {
     cudaError_t e = cudaMemset2DAsync(C, sizeof(float) * (size_t)ldc, 0, sizeof(float) * (size_t)N, (size_t)M, st);
     if (e != cudaSuccess) return cuda_status(e, "screened_spmm: zero C");
   }
@@ -331,8 +389,11 @@ extern "C" int trnsparse_screened_spmm(int64_t M, int64_t K, int64_t N, const fl
   if (rc) return rc;
   rc = make_tmap_2d(&bl, bt_lo, dt, (uint64_t)k_pad, (uint64_t)N, (uint64_t)k_pad * 4, 32, (uint32_t)bn);
   if (rc) return rc;
+  CUtensorMap cm;
+  rc = make_tmap_2d(&cm, C, dt, (uint64_t)N, (uint64_t)M, (uint64_t)ldc * 4, 32, 32);
+  if (rc) return rc;
   const float t = static_cast<float>(sqrt(threshold));
   const float* qv = bounds_kind == 1 ? bounds : nullptr;
-  return bn == 128 ? launch_sc<128>(ta, tq, bh, bl, qv, bounds_kind, t, M, K, N, (int)nkb, nsplit, C, ldc, st)
-                   : launch_sc<256>(ta, tq, bh, bl, qv, bounds_kind, t, M, K, N, (int)nkb, nsplit, C, ldc, st);
+  return bn == 128 ? launch_sc<128>(ta, tq, bh, bl, cm, qv, bounds_kind, t, M, K, N, (int)nkb, (int)nt, grid, st)
+                   : launch_sc<256>(ta, tq, bh, bl, cm, qv, bounds_kind, t, M, K, N, (int)nkb, (int)nt, grid, st);
 }

@@ -11,7 +11,6 @@ compute path and no backend switch.
 from __future__ import annotations
 
 import ctypes
-import math
 import os
 
 import torch
@@ -505,11 +504,47 @@ def _bsr_transpose(A: BSRMatrix, dev: torch.device) -> BSRMatrix:
     return AT
 
 
+def _nt_tc(X: torch.Tensor, Y: torch.Tensor, tiles: torch.Tensor | None, out: torch.Tensor, out_rows: int = 0,
+           out_cols: int = 0, mask_kind: int = 0, bounds: torch.Tensor | None = None, ldq: int = 0,
+           threshold: float = 0.0) -> None:
+    """``trnsparse_nt_tc``: 128 x 128 tiles of X Y^T on the tensor cores (X, Y row-major,
+    contraction along the rows; fp32 3xTF32 or bf16)."""
+    dev = X.device
+    code = _lib.dtype_code(X.dtype)
+    mx, K = X.shape
+    my = Y.shape[0]
+    ws_bytes = _lib.raw("trnsparse_nt_tc_workspace_size")(mx, my, K, code)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    n_tiles = tiles.shape[0] if tiles is not None else 0
+    with torch.cuda.device(dev):
+        _lib.call("trnsparse_nt_tc", mx, my, K, code, X.data_ptr(), X.stride(0), Y.data_ptr(), Y.stride(0),
+                  _lib.ptr(tiles), n_tiles, out.data_ptr(), out.stride(0) if out.dim() == 2 else out.shape[-1],
+                  _lib.dtype_code(out.dtype), out_rows, out_cols, mask_kind, _lib.ptr(bounds), ldq, float(threshold),
+                  ws.data_ptr(), ws_bytes, _lib.stream_handle(dev))
+
+
 def _bsr_blocks_grad(A: BSRMatrix, dC: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     """dblocks[k] = dC[rows of block-row i] @ B[rows of block-column j]^T for
-    stored block k = (i, j): one batched GEMM over the gathered row blocks."""
+    stored block k = (i, j) (the reference's _BSRSpMMFunction.backward,
+    nki/dispatch.py:331-369). Block size 128 with float32 / bfloat16 blocks:
+    one tensor-core launch over the stored blocks (``trnsparse_nt_tc``, the
+    dC and B tiles read in place); other block sizes: a batched product over
+    gathered row blocks."""
     b = A.block_size
-    dev = dC.device
+    dev = dC.device if dC.is_cuda else _dev_of(B)
+    if b == 128 and A.dtype in (torch.float32, torch.bfloat16):
+        lay = A.device_layout(dev)
+        tiles = lay.get("block_tiles")
+        if tiles is None:
+            rp, ci = lay["host_row_ptr"], lay["host_col_idx"]
+            rows = torch.repeat_interleave(torch.arange(rp.numel() - 1), rp[1:] - rp[:-1])
+            tiles = lay["block_tiles"] = torch.stack([rows, ci], 1).to(device=dev, dtype=torch.int32).contiguous()
+        X = _on(dC, dev, A.dtype)
+        Y = _on(B, dev, A.dtype)
+        out = torch.empty(A.n_blocks, b, b, dtype=A.dtype, device=dev)
+        if A.n_blocks:
+            _nt_tc(X, Y, tiles, out)
+        return out.to(A.blocks.device)
     R = A.block_row_ptrs.numel() - 1
     Cn = -(-A.shape[1] // b)
     k = dC.shape[1]
@@ -604,15 +639,18 @@ class _ScreenedFn(torch.autograd.Function):
             Qt = Q if Q.dim() == 1 else Q.t().contiguous()  # the 1-D mask is symmetric
             dB = _screened_impl(A.detach().t().contiguous(), Qt, dC.contiguous(), thr).to(B.device)
         if ctx.needs_input_grad[0]:
-            dev = dC.device
-            Qd = Q.to(device=dev, dtype=torch.float32)
-            t = float(torch.tensor(math.sqrt(thr), dtype=torch.float32))  # fp32(sqrt(threshold)), as the kernel
-            if Qd.dim() == 1:
-                q = torch.sqrt(torch.abs(Qd))
-                mask = q.unsqueeze(1) * q.unsqueeze(0) > t
-            else:
-                mask = Qd > t
-            dA = ((dC.float() @ B.to(dev).float().t()) * mask).to(A.device)
+            # dA = (dC B^T) o mask, one tensor-core launch with the mask in its epilogue
+            dev = dC.device if dC.is_cuda else _dev_of(B)
+            X = _on(dC, dev, torch.float32)
+            Y = _on(B, dev, torch.float32)
+            Qd = _on(Q, dev, torch.float32)
+            M, K = A.shape
+            Kp = -(-K // 4) * 4
+            dA = torch.empty(M, Kp, dtype=torch.float32, device=dev)
+            _nt_tc(X, Y, None, dA, M, K, 1 if Qd.dim() == 1 else 2, Qd, Qd.stride(0) if Qd.dim() == 2 else 0, thr)
+            if Kp != K:
+                dA = dA[:, :K].contiguous()
+            dA = dA.to(A.device)
         return dA, dB, None, None
 
 
@@ -647,13 +685,16 @@ def _screened_impl(A: torch.Tensor, diag_integrals: torch.Tensor, B: torch.Tenso
             Qp = torch.zeros(M, Kp, device=dev)
             Qp[:, :K] = Qd
             Qd = Qp
-    out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    Np = -(-N // 4) * 4  # C rows 16-byte aligned for the kernel's TMA stores
+    out = torch.empty(M, Np, dtype=torch.float32, device=dev)
     ws_bytes = _lib.raw("trnsparse_screened_spmm_workspace_size")(K, N)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         _lib.call("trnsparse_screened_spmm", M, K, N, Ad.data_ptr(), Ad.shape[1], Qd.data_ptr(), kind,
-                  Qd.shape[-1] if kind == 2 else 0, float(threshold), Bd.data_ptr(), N, out.data_ptr(), N,
+                  Qd.shape[-1] if kind == 2 else 0, float(threshold), Bd.data_ptr(), N, out.data_ptr(), Np,
                   ws.data_ptr(), ws_bytes, _lib.stream_handle(dev))
+    if Np != N:
+        out = out[:, :N].contiguous()
     return _back(out, B)
 
 
