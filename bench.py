@@ -330,8 +330,9 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
     is gathered to rank 0 and compared (relative 2-norm error) with the
     unsharded single-GPU ``cg_bsr`` solve of the same matrix, right-hand side
     and iteration count, which rank 0 also times in the same run
-    (``us_per_iteration_single_gpu``); ``speedup_vs_1gpu`` = single-GPU time
-    per iteration / sharded time per iteration."""
+    (``us_per_iteration_single_gpu``: the faster of the public ``cg_bsr`` and
+    the one-rank cgcg solve in a CUDA graph, named in ``single_gpu_solver``);
+    ``speedup_vs_1gpu`` = that time per iteration / sharded time per iteration."""
     import torch.distributed as dist
 
     import trnsparse_b200 as ts
@@ -354,6 +355,26 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
         torch.cuda.synchronize()
         single = {"x": x1.clone(), "ms": a.elapsed_time(e), "rel": rel1}
         del M, bd
+    # the best single-GPU solve of the same problem: the one-rank cgcg solve captured in a
+    # CUDA graph like the sharded ones (every rank takes part in creating the group)
+    one = dist.new_group([0])
+    if rank == 0:
+        try:
+            sh1 = D.shard_bsr(A, 0, 1)
+            cg1 = D.ShardedCG(sh1, b.cuda(), tol=0.0, max_iter=iters, graph=True, transport="cgcg", group=one)
+            cg1.run()
+            torch.cuda.synchronize()
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            cg1.run()
+            e.record()
+            torch.cuda.synchronize()
+            single["ms_cgcg1"] = a.elapsed_time(e)
+            single["exec_cgcg1"] = cg1.executed_iterations()
+            cg1.close()
+        except Exception as exc:  # keep the cg_bsr baseline if the one-rank solve cannot run
+            single["cgcg1_error"] = f"{type(exc).__name__}: {exc}"[:120]
+    dist.barrier()
     sh = D.shard_bsr(A, rank, ws)
     bl = b[sh.r0 * 128 : sh.r1 * 128].cuda()
     devs = [None] * ws
@@ -384,8 +405,14 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
                "scaling": "strong", "rel_residual": rel}
         if rank == 0:
             err = float((xg.double() - single["x"].double()).norm() / single["x"].double().norm())
-            us1 = single["ms"] / max(executed, 1) * 1e3
+            us_api = single["ms"] / max(executed, 1) * 1e3
+            us1, src = us_api, "cg_bsr"
+            if "ms_cgcg1" in single:
+                us_g = single["ms_cgcg1"] / max(single["exec_cgcg1"], 1) * 1e3
+                if us_g < us1:
+                    us1, src = us_g, "one-rank cgcg, CUDA graph"
             row.update({"rel_err_vs_single_gpu": err, "us_per_iteration_single_gpu": round(us1, 2),
+                        "single_gpu_solver": src, "us_per_iteration_cg_bsr_api": round(us_api, 2),
                         "speedup_vs_1gpu": round(us1 / (ms / max(executed, 1) * 1e3), 3)})
         out[f"config5_cg_sharded_{transport}"] = row
     return out
