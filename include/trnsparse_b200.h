@@ -200,8 +200,9 @@ TRNSPARSE_API int trnsparse_bsr_spmm_simt(int64_t m, int64_t n, int b, int64_t n
  *   dtype F32: 3xTF32 (hi*hi + hi*lo + lo*hi); blocks_hi/blocks_lo are the
  *              tf32 split of the blocks (trnsparse_bsr_split_tf32); B, C fp32.
  *   dtype BF16: blocks_hi and B are bf16 (blocks_lo unused).
- * c_dtype: F32, or BF16 (bf16 inputs and needs_zero == 0 only: the fp32
- * accumulators are rounded once, in the epilogue).
+ * c_dtype: F32, or BF16 (bf16 inputs only: each unit's fp32 accumulator is
+ * rounded once in the epilogue; units of a split block-row add their rounded
+ * partial sums into the cleared bf16 C).
  * plan (device memory): the work schedule written on the host by
  * trnsparse_bsr_spmm_tc_plan for this matrix's row pointers, k, bn and grid
  * (CTA count; cache it per matrix). needs_zero: that call's flag (C is

@@ -98,8 +98,6 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
   auto a_tile = [&](int s, int part) { return sp_smem + s * Lay::kStage + part * Lay::kA; };
   auto b_tile = [&](int s, int part) { return sp_smem + s * Lay::kStage + Cfg::kParts * Lay::kA + part * Lay::kB; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int u_begin = plan[blockIdx.x], u_end = plan[blockIdx.x + 1];
-  const int4* units = reinterpret_cast<const int4*>(plan + plan_head(grid));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -124,8 +122,11 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();  // the set-up above overlapped the previous kernel (the B split, the C clearing)
   const uint32_t tmem = B.tmem_slot;
   volatile int* abort_flag = &B.abort_flag;
+  const int u_begin = plan[blockIdx.x], u_end = plan[blockIdx.x + 1];
+  const int4* units = reinterpret_cast<const int4*>(plan + plan_head(grid));
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -259,7 +260,7 @@ bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_const
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && row0 < m && ok) {
-          if (!OUT_BF16 && reduce)
+          if (reduce)  // fp32 or bf16 adds, per the C tensor map's type
             tma_reduce_add_2d(&tc, stage, n0 + p * PW, static_cast<int>(row0));
           else
             tma_store_2d(&tc, stage, n0 + p * PW, static_cast<int>(row0));
@@ -288,8 +289,8 @@ int launch_sp(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap&
   auto kern = bsr_spmm_tc_kernel<KIND, BN, OUT_BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kSmem);
   if (e != cudaSuccess) return cuda_status(e, "bsr_spmm_tc: set smem");
-  kern<<<grid, kSpThreads, Lay::kSmem, st>>>(ahi, alo, bhi, blo, cm, plan, grid, col_idx, m, k);
-  TSB_CHECK_LAUNCH("bsr_spmm_tc launch");
+  e = launch_pdl(kern, dim3(grid), dim3(kSpThreads), Lay::kSmem, st, ahi, alo, bhi, blo, cm, plan, grid, col_idx, m, k);
+  if (e != cudaSuccess) return cuda_status(e, "bsr_spmm_tc launch");
   return debug_sync(st, "bsr_spmm_tc: main kernel (sync)");
 }
 
@@ -418,8 +419,8 @@ extern "C" int trnsparse_bsr_spmm_tc(int64_t m, int64_t n, int64_t n_blocks, con
   TSB_REQUIRE(bn == 128 || bn == 256, "bsr_spmm_tc: bn must be 128 or 256");
   if (m == 0 || k == 0) return TRNSPARSE_OK;
   TSB_REQUIRE(C && plan && grid > 0, "bsr_spmm_tc: null pointer or empty plan");
-  TSB_REQUIRE(c_dtype == TRNSPARSE_F32 || (c_dtype == TRNSPARSE_BF16 && dtype == TRNSPARSE_BF16 && !needs_zero),
-              "bsr_spmm_tc: C is F32, or BF16 for BF16 inputs with a plan that splits no block-row");
+  TSB_REQUIRE(c_dtype == TRNSPARSE_F32 || (c_dtype == TRNSPARSE_BF16 && dtype == TRNSPARSE_BF16),
+              "bsr_spmm_tc: C is F32, or BF16 for BF16 inputs");
   const bool c_bf16 = c_dtype == TRNSPARSE_BF16;
   TSB_REQUIRE((ldc * (c_bf16 ? 2 : 4)) % 16 == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0,
               "bsr_spmm_tc: C must be 16-byte aligned with 16-byte rows");
@@ -430,7 +431,8 @@ extern "C" int trnsparse_bsr_spmm_tc(int64_t m, int64_t n, int64_t n_blocks, con
   TSB_REQUIRE(ws && ws_bytes >= need, "bsr_spmm_tc: workspace too small (%zu < %zu)", ws_bytes, need);
   cudaStream_t st = as_stream(stream);
   if (needs_zero) {
-    cudaError_t e = cudaMemset2DAsync(C, sizeof(float) * (size_t)ldc, 0, sizeof(float) * (size_t)k, (size_t)m, st);
+    const size_t es_c = c_dtype == TRNSPARSE_BF16 ? 2 : 4;
+    cudaError_t e = cudaMemset2DAsync(C, es_c * (size_t)ldc, 0, es_c * (size_t)k, (size_t)m, st);
     if (e != cudaSuccess) return cuda_status(e, "bsr_spmm_tc: zero C");
   }
   const bool f32 = dtype == TRNSPARSE_F32;

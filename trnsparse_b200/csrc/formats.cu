@@ -377,6 +377,161 @@ __global__ void coo_scatter_kernel(int64_t nnz, int64_t m, int64_t n, const long
   }
 }
 
+// COO -> CSR for up to kBucketRows * kMaxBuckets rows, in buckets of kBucketRows
+// consecutive rows, with no per-entry global atomic (a radix-partition scheme):
+//   count      CTA c counts its chunk of entries per bucket in shared memory (and
+//              flags out-of-range indices) and writes the counts to column c of a
+//              bucket-major count matrix
+//   scan       one exclusive scan of that matrix gives every (bucket, CTA) pair its
+//              offset; bucket b's region starts at the offset of (b, 0)
+//   partition  CTA c writes its entries to its offsets as (row within the bucket,
+//              col << 32 | entry index), ranks from shared-memory atomics
+//   rows       a CTA per bucket: row histogram and scan in shared memory write the
+//              bucket's row pointers, then each entry goes to its row's cursor
+// Entry order inside a row is arbitrary after this; the per-row sort of the
+// (col << 32 | entry index) keys gives the stable (row, col) order.
+constexpr int kBucketRows = 4096;
+constexpr int kMaxBuckets = 4096;              // rows up to 2^24 take this path
+constexpr int kPartChunk = 8192;               // entries per CTA in the count / partition passes
+constexpr int64_t kMaxCountCells = 1ll << 24;  // cells of the count matrix (the chunk grows past it)
+
+__host__ __device__ inline int64_t coo_chunk(int64_t nnz, int nb) {
+  const int64_t per = kMaxCountCells / nb;  // CTAs the matrix can hold
+  const int64_t c = (nnz + per - 1) / per;
+  return c > kPartChunk ? c : kPartChunk;
+}
+
+__device__ __forceinline__ bool coo_ok(long long r, long long c, int64_t m, int64_t n) {
+  return r >= 0 && r < m && c >= 0 && c < n;
+}
+
+__global__ void __launch_bounds__(256) coo_bucket_count_kernel(int64_t nnz, int64_t m, int64_t n, int nb,
+                                                               int64_t chunk, const long long* __restrict__ rows,
+                                                               const long long* __restrict__ cols,
+                                                               long long* __restrict__ cm, int* __restrict__ bad) {
+  __shared__ int cnt[kMaxBuckets];
+  const int64_t G = gridDim.x, c = blockIdx.x;
+  const int64_t c0 = c * chunk, c1 = c0 + chunk < nnz ? c0 + chunk : nnz;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) cnt[b] = 0;
+  __syncthreads();
+  int flag = 0;
+  for (int64_t e0 = c0 + threadIdx.x; e0 < c1; e0 += 4 * blockDim.x) {
+    long long r[4], k[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t e = e0 + u * blockDim.x;
+      r[u] = e < c1 ? rows[e] : 0;
+      k[u] = e < c1 ? cols[e] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (e0 + u * blockDim.x >= c1) continue;
+      if (coo_ok(r[u], k[u], m, n)) atomicAdd(&cnt[r[u] / kBucketRows], 1);
+      else flag = 1;
+    }
+  }
+  if (flag) atomicExch(bad, 1);
+  __syncthreads();
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) cm[1 + b * G + c] = cnt[b];
+}
+
+__global__ void __launch_bounds__(256) coo_partition_kernel(int64_t nnz, int64_t m, int64_t n, int nb, int64_t chunk,
+                                                            const long long* __restrict__ rows,
+                                                            const long long* __restrict__ cols,
+                                                            const long long* __restrict__ cm,
+                                                            int* __restrict__ prow,
+                                                            unsigned long long* __restrict__ pkey) {
+  __shared__ int cnt[kMaxBuckets];
+  __shared__ long long base[kMaxBuckets];
+  const int64_t G = gridDim.x, c = blockIdx.x;
+  const int64_t c0 = c * chunk, c1 = c0 + chunk < nnz ? c0 + chunk : nnz;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    cnt[b] = 0;
+    base[b] = cm[b * G + c];
+  }
+  __syncthreads();
+  for (int64_t e0 = c0 + threadIdx.x; e0 < c1; e0 += 4 * blockDim.x) {
+    long long r[4], k[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t e = e0 + u * blockDim.x;
+      r[u] = e < c1 ? rows[e] : -1;
+      k[u] = e < c1 ? cols[e] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (!coo_ok(r[u], k[u], m, n)) continue;
+      const int b = static_cast<int>(r[u] / kBucketRows);
+      const long long p = base[b] + atomicAdd(&cnt[b], 1);
+      prow[p] = static_cast<int>(r[u] - static_cast<long long>(b) * kBucketRows);
+      pkey[p] = (static_cast<unsigned long long>(k[u]) << 32) |
+                static_cast<unsigned long long>(e0 + u * blockDim.x);
+    }
+  }
+}
+
+// bucket b's entries: [cm[b * G], cm[(b + 1) * G]) (the last bound is cm[nb * G], the total)
+__global__ void __launch_bounds__(256) coo_bucket_rows_kernel(int64_t m, int nb, int64_t G,
+                                                              const long long* __restrict__ cm,
+                                                              const int* __restrict__ prow,
+                                                              const unsigned long long* __restrict__ pkey,
+                                                              long long* __restrict__ row_ptr,
+                                                              unsigned long long* __restrict__ keys) {
+  __shared__ unsigned int cur[kBucketRows];
+  __shared__ unsigned int wsum[8];
+  constexpr int kPer = kBucketRows / 256;  // bins per thread in the scan
+  for (int b = blockIdx.x; b < nb; b += gridDim.x) {
+    const int64_t r0 = static_cast<int64_t>(b) * kBucketRows;
+    const int nr = static_cast<int>(m - r0 < kBucketRows ? m - r0 : kBucketRows);
+    const long long s = cm[b * G], e = cm[(b + 1) * G];
+    const unsigned int len = static_cast<unsigned int>(e - s);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kBucketRows; i += blockDim.x) cur[i] = 0;
+    __syncthreads();
+    for (unsigned int i = threadIdx.x; i < len; i += blockDim.x) atomicAdd(&cur[prow[s + i]], 1u);
+    __syncthreads();
+    unsigned int v[kPer], tot = 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      v[q] = cur[threadIdx.x * kPer + q];
+      tot += v[q];
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    unsigned int inc = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned int y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
+    }
+    if (lane == 31) wsum[w] = inc;
+    __syncthreads();
+    unsigned int off = inc - tot;
+    for (int k = 0; k < w; ++k) off += wsum[k];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int i = threadIdx.x * kPer + q;
+      cur[i] = off;
+      if (i < nr) row_ptr[r0 + i] = s + off;
+      off += v[q];
+    }
+    if (r0 + nr == m && threadIdx.x == 0) row_ptr[m] = e;
+    __syncthreads();
+    for (unsigned int i0 = threadIdx.x; i0 < len; i0 += 4u * blockDim.x) {
+      int rr[4];
+      unsigned long long kk[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const unsigned int i = i0 + u * blockDim.x;
+        rr[u] = i < len ? prow[s + i] : -1;
+        kk[u] = i < len ? pkey[s + i] : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (rr[u] >= 0) keys[s + atomicAdd(&cur[rr[u]], 1u)] = kk[u];
+    }
+  }
+}
+
 // entry of a sorted key: column and source index -> outputs
 __device__ __forceinline__ void coo_emit(unsigned long long key, long long p, const uint8_t* __restrict__ vals_in,
                                          int esz, long long* __restrict__ cols_out, uint8_t* __restrict__ vals_out) {
@@ -752,7 +907,16 @@ extern "C" int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A
 // ---------------------------------------------------------------- COO -> CSR
 extern "C" size_t trnsparse_coo_to_csr_workspace_size(int64_t m, int64_t nnz) {
   if (m < 0 || nnz < 0) return 0;
-  return sizeof(unsigned long long) * (size_t)(2 * nnz + 3 * m + 1) + scan_ws_bytes(m) + 32;
+  // keys, keys2, cursors, scan partials, row lists, counters; then, for the bucketed
+  // path, the local rows (int32 per entry), the count matrix and its scan partials
+  size_t extra = 0;
+  if (m > 0 && m <= static_cast<int64_t>(kBucketRows) * kMaxBuckets) {
+    const int nb = static_cast<int>((m + kBucketRows - 1) / kBucketRows);
+    const int64_t chunk = coo_chunk(nnz, nb);
+    const int64_t G = nnz > 0 ? (nnz + chunk - 1) / chunk : 1;
+    extra = sizeof(int) * (size_t)nnz + 16 + sizeof(long long) * (size_t)(nb * G + 1) + scan_ws_bytes(nb * G);
+  }
+  return sizeof(unsigned long long) * (size_t)(2 * nnz + 3 * m + 1) + scan_ws_bytes(m) + 32 + extra;
 }
 
 extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const long long* rows, const long long* cols,
@@ -775,20 +939,47 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
   unsigned long long* n_mid = reinterpret_cast<unsigned long long*>(long_rows + m);
   unsigned long long* n_long = n_mid + 1;
   int* bad = reinterpret_cast<int*>(n_long + 1);
-  cudaError_t e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(n_mid, 0, 24, st);  // n_mid, n_long and bad
+  cudaError_t e = cudaMemsetAsync(n_mid, 0, 24, st);  // n_mid, n_long and bad
   if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
-  if (nnz > 0) {
-    coo_count_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols,
-                                                        reinterpret_cast<unsigned long long*>(row_ptr), bad);
-    TSB_CHECK_LAUNCH("coo_to_csr: count");
+  if (m > 0 && m <= static_cast<int64_t>(kBucketRows) * kMaxBuckets) {
+    // bucketed path: no per-entry global atomic (see coo_bucket_*_kernel)
+    const int nb = static_cast<int>((m + kBucketRows - 1) / kBucketRows);
+    const int64_t chunk = coo_chunk(nnz, nb);
+    const int64_t G = nnz > 0 ? (nnz + chunk - 1) / chunk : 1;
+    int* prow = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(n_mid) + 32);  // past n_mid, n_long, bad
+    long long* cm = reinterpret_cast<long long*>(
+        (reinterpret_cast<uintptr_t>(prow + nnz) + 15) & ~static_cast<uintptr_t>(15));  // nb * G + 1 cells
+    long long* cpart = cm + nb * G + 1;                                                   // its scan partials
+    if (nnz > 0) {
+      coo_bucket_count_kernel<<<(unsigned)G, 256, 0, st>>>(nnz, m, n, nb, chunk, rows, cols, cm, bad);
+      TSB_CHECK_LAUNCH("coo_to_csr: bucket count");
+    } else {
+      e = cudaMemsetAsync(cm, 0, sizeof(long long) * (nb * G + 1), st);
+      if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear counts");
+    }
+    int rc = exclusive_scan(cm, nb * G, cpart, st);
+    if (rc) return rc;
+    if (nnz > 0)
+      coo_partition_kernel<<<(unsigned)G, 256, 0, st>>>(nnz, m, n, nb, chunk, rows, cols, cm, prow, keys2);
+    coo_bucket_rows_kernel<<<(unsigned)(nb < 32 * sm_count() ? nb : 32 * sm_count()), 256, 0, st>>>(
+        m, nb, G, cm, prow, keys2, row_ptr, keys);
+    TSB_CHECK_LAUNCH("coo_to_csr: bucket rows");
+    if (nnz == 0) return TRNSPARSE_OK;
+  } else {
+    e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
+    if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
+    if (nnz > 0) {
+      coo_count_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols,
+                                                          reinterpret_cast<unsigned long long*>(row_ptr), bad);
+      TSB_CHECK_LAUNCH("coo_to_csr: count");
+    }
+    int rc = exclusive_scan(row_ptr, m, part, st);
+    if (rc) return rc;
+    if (nnz == 0 || m == 0) return TRNSPARSE_OK;
+    e = cudaMemcpyAsync(cursor, row_ptr, sizeof(long long) * m, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: cursors");
+    coo_scatter_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols, cursor, keys);
   }
-  int rc = exclusive_scan(row_ptr, m, part, st);
-  if (rc) return rc;
-  if (nnz == 0 || m == 0) return TRNSPARSE_OK;
-  e = cudaMemcpyAsync(cursor, row_ptr, sizeof(long long) * m, cudaMemcpyDeviceToDevice, st);
-  if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: cursors");
-  coo_scatter_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols, cursor, keys);
   coo_sort_tiny_kernel<<<grid_for(m, 256), 256, 0, st>>>(m, row_ptr, keys, (const uint8_t*)values, esz, cols_out,
                                                         (uint8_t*)values_out, mid_rows, n_mid, long_rows, n_long);
   coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, (const uint8_t*)values, esz,

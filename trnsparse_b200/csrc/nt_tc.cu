@@ -123,6 +123,7 @@ nt_tc_kernel(const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();  // the set-up above overlapped the previous kernel (the operand split)
   const uint32_t tmem = Bs.tmem_slot;
   volatile int* abort_flag = &Bs.abort_flag;
 
@@ -267,6 +268,7 @@ nt_tc_kernel(const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ 
 // rows x Kp matrices, zero past column K.
 __global__ void split_pad_kernel(int64_t rows, int64_t K, const float* __restrict__ src, int64_t ld, int64_t Kp,
                                  float* __restrict__ hi, float* __restrict__ lo) {
+  grid_dep_launch();
   const int64_t total = rows * Kp;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -298,9 +300,9 @@ int launch_nt(const CUtensorMap& xh, const CUtensorMap& xl, const CUtensorMap& y
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
   if (e != cudaSuccess) return cuda_status(e, "nt_tc: set smem");
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
-  kern<<<grid, kNtThreads, Cfg::kSmem, st>>>(xh, xl, yh, yl, om, tiles, n_tiles, nj, n_chunks, out_rows, out_cols,
-                                            q_vec, qmat, ldq, t);
-  TSB_CHECK_LAUNCH("nt_tc launch");
+  e = launch_pdl(kern, dim3(grid), dim3(kNtThreads), Cfg::kSmem, st, xh, xl, yh, yl, om, tiles, n_tiles, nj, n_chunks,
+                 out_rows, out_cols, q_vec, qmat, ldq, t);
+  if (e != cudaSuccess) return cuda_status(e, "nt_tc launch");
   return debug_sync(st, "nt_tc: main kernel (sync)");
 }
 

@@ -122,6 +122,7 @@ screened_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();  // the set-up above overlapped the previous kernel (the operand split)
   const uint32_t tmem = Bs.tmem_slot;
   volatile int* abort_flag = &Bs.abort_flag;
 
@@ -319,8 +320,9 @@ int launch_sc(const CUtensorMap& ta, const CUtensorMap& tq, const CUtensorMap& b
   auto kern = screened_tc_kernel<BN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kSmem);
   if (e != cudaSuccess) return cuda_status(e, "screened_tc: set smem");
-  kern<<<grid, kScThreads, Lay::kSmem, st>>>(ta, tq, bhi, blo, cm, q_vec, mode, t, M, K, N, nkb, nt);
-  TSB_CHECK_LAUNCH("screened_tc launch");
+  e = launch_pdl(kern, dim3(grid), dim3(kScThreads), Lay::kSmem, st, ta, tq, bhi, blo, cm, q_vec, mode, t, M, K, N, nkb,
+                 nt);
+  if (e != cudaSuccess) return cuda_status(e, "screened_tc launch");
   return debug_sync(st, "screened_tc: main kernel (sync)");
 }
 

@@ -185,6 +185,15 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while the kernel before it in the
+// stream still runs; grid_dep_wait() blocks until that kernel has completed
+// and its writes are visible, so everything before it may only touch memory
+// the previous kernel does not write. grid_dep_launch() lets the dependent
+// kernel start early. Both are no-ops without the attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 }  // namespace tsb

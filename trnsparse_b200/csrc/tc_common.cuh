@@ -8,6 +8,8 @@
 #include <cuda_bf16.h>
 #include <stdlib.h>
 
+#include <utility>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -66,6 +68,7 @@ template <bool SPLIT, typename E>
 __global__ void transpose_b_kernel(int64_t n, int64_t k, const E* __restrict__ B, int64_t ldb, int64_t n_pad,
                                    E* __restrict__ hi, E* __restrict__ lo) {
   __shared__ float tile[32][33];
+  grid_dep_launch();  // the tensor-core kernel after it may start its set-up now
   const int64_t nb = static_cast<int64_t>(blockIdx.x) * 32, kb = static_cast<int64_t>(blockIdx.y) * 32;
   for (int r = threadIdx.y; r < 32; r += blockDim.y) {
     const int64_t nn = nb + r, kk = kb + threadIdx.x;
@@ -93,6 +96,24 @@ __global__ void transpose_b_kernel(int64_t n, int64_t k, const E* __restrict__ B
 }
 
 inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Launches `kern` with programmatic stream serialization (the kernel calls
+// grid_dep_wait() before touching memory the previous kernel writes), so its
+// launch latency and set-up overlap the previous kernel's tail.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
                  uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows,

@@ -387,7 +387,9 @@ def _bsr_spmm_impl(A: BSRMatrix, B: torch.Tensor) -> torch.Tensor:
             bf16 = A.dtype == torch.bfloat16
             Bd = _on(B, dev, torch.bfloat16 if bf16 else torch.float32)
             plan, grid, zero, bn = _tc_plan(A, lay, dev, k)
-            direct = bf16 and not zero  # bf16 C straight from the epilogue
+            # bf16: C straight from the epilogue in bf16 (split block-rows add their partial sums
+            # in bf16, as the reference's bf16 block loop accumulates in the blocks' dtype)
+            direct = bf16
             kp = -(-k // 8) * 8 if direct else -(-k // 4) * 4  # 16-byte C rows for the TMA stores
             out = torch.empty(m, kp, dtype=torch.bfloat16 if direct else torch.float32, device=dev)
             if bf16:
