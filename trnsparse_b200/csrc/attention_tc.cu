@@ -89,6 +89,16 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Tile t -> (head, query block). Head-minor order: the CTAs running at the same time work
+// on all heads at once, so the K/V tiles of one head (the global key blocks above all,
+// which every query block of the head reads) are not all fetched at the same moment
+// (config 4: 0.212 -> 0.207 ms; query blocks in descending order measured slower).
+__device__ __forceinline__ void at_tile(int t, int m_tiles, int n_tiles, int& head, int& qb) {
+  const int heads = n_tiles / m_tiles;
+  qb = t / heads;
+  head = t - qb * heads;
+}
+
 // Walks this CTA's tiles (round robin over the grid), skipping empty block-rows,
 // and the stored key blocks of each.
 struct TileCursor {
@@ -98,8 +108,7 @@ struct TileCursor {
   bool valid;
   __device__ void seek(int from) {
     for (t = from; t < n_tiles; t += stride) {
-      head = t / m_tiles;
-      qb = t - head * m_tiles;
+      at_tile(t, m_tiles, n_tiles, head, qb);
       e0 = row_ptr[qb];
       nb = row_ptr[qb + 1] - e0;
       if (nb > 0) {
@@ -305,7 +314,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       return true;
     };
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-      const int head = t / m_tiles, qb = t - head * m_tiles;
+      int head, qb;
+      at_tile(t, m_tiles, n_tiles, head, qb);
       const int nb = row_ptr[qb + 1] - row_ptr[qb];
       if (nb <= 0 || !ok) {  // an empty block-row is zero (as in the reference)
         uint4* orow = reinterpret_cast<uint4*>(O + static_cast<int64_t>(head * seq + qb * 128 + r) * HD +
