@@ -324,14 +324,18 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
     2048-block-row matrix is split across the ranks), each transport (cgcg:
     one reduction per iteration in one cooperative launch; coop / fused /
     peer / nccl: the reference's two reductions), whole solve captured in one
-    CUDA graph, ``iters`` iterations with tol 0, time = max over ranks.
+    CUDA graph, ``iters`` iterations with tol 0. ``us_per_iteration`` is the
+    device time of the graph replay (CUDA events on the solve's stream around
+    ``launch()``), max over ranks; ``us_per_iteration_with_readback`` also
+    holds the host read of the status words (``result()``).
 
     Every row carries its own correctness check and speed-up: the sharded x
     is gathered to rank 0 and compared (relative 2-norm error) with the
     unsharded single-GPU ``cg_bsr`` solve of the same matrix, right-hand side
     and iteration count, which rank 0 also times in the same run
-    (``us_per_iteration_single_gpu``: the faster of the public ``cg_bsr`` and
-    the one-rank cgcg solve in a CUDA graph, named in ``single_gpu_solver``);
+    (``us_per_iteration_single_gpu``: the faster of the public ``cg_bsr`` call
+    and the one-rank cgcg solve in a CUDA graph timed like the sharded one,
+    named in ``single_gpu_solver``);
     ``speedup_vs_1gpu`` = that time per iteration / sharded time per iteration."""
     import torch.distributed as dist
 
@@ -366,9 +370,9 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
             torch.cuda.synchronize()
             a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            cg1.run()
+            cg1.launch()
             e.record()
-            torch.cuda.synchronize()
+            cg1.result()
             single["ms_cgcg1"] = a.elapsed_time(e)
             single["exec_cgcg1"] = cg1.executed_iterations()
             cg1.close()
@@ -386,12 +390,15 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
             cg.run()
             torch.cuda.synchronize()
             dist.barrier()
-            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a, e, f = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             a.record()
-            x, it, rel = cg.run()
+            cg.launch()
             e.record()
+            x, it, rel = cg.result()
+            f.record()
             torch.cuda.synchronize()
             ms = max_over_ranks(a.elapsed_time(e), ws)
+            ms_rb = max_over_ranks(a.elapsed_time(f), ws)
             executed = cg.executed_iterations()
             xg = _gather_x(x, ws)
             cg.close()
@@ -399,7 +406,9 @@ def run_sharded_cg(ws: int, rank: int, local: int, pk: dict,
             out[f"config5_cg_sharded_{transport}"] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
             continue
         nb = A.n_blocks * 128 * 128 * 4
-        row = {"us_per_iteration": round(ms / max(executed, 1) * 1e3, 2), "executed_iterations": executed,
+        row = {"us_per_iteration": round(ms / max(executed, 1) * 1e3, 2),
+               "us_per_iteration_with_readback": round(ms_rb / max(executed, 1) * 1e3, 2),
+               "executed_iterations": executed,
                "max_iter": iters, "ranks": ws, "gpus_active": len(set(devs)),
                "matrix_GB/s_aggregate": round(nb * executed / (ms * 1e-3) / 1e9, 1),
                "scaling": "strong", "rel_residual": rel}

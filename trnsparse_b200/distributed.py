@@ -395,11 +395,21 @@ class ShardedCG:
                  self.n_sends, lib.stream_handle(self.dev))
 
     def run(self) -> tuple[torch.Tensor, int, float]:
+        self.launch()
+        return self.result()
+
+    def launch(self) -> None:
+        """Enqueue the solve on this rank's stream (one graph replay when captured; the
+        uncaptured transports also poll the device between chunks of iterations)."""
         with torch.cuda.device(self.dev):
             if self.graph is not None:
                 self.graph.replay()
             else:
                 self._solve(check=True)
+
+    def result(self) -> tuple[torch.Tensor, int, float]:
+        """Wait for the solve enqueued by ``launch`` and read its status: this rank's
+        slice of x, the iteration count and the relative residual."""
         head = self.ws[:64].cpu()
         if head[8:12].view(torch.int32).item() == 5:
             raise RuntimeError("sharded CG: an exchange with a peer timed out (device error word set)")
