@@ -384,16 +384,25 @@ __global__ void coo_scatter_kernel(int64_t nnz, int64_t m, int64_t n, const long
 //              bucket-major count matrix
 //   scan       one exclusive scan of that matrix gives every (bucket, CTA) pair its
 //              offset; bucket b's region starts at the offset of (b, 0)
-//   partition  CTA c writes its entries to its offsets as (row within the bucket,
-//              col << 32 | entry index), ranks from shared-memory atomics
-//   rows       a CTA per bucket: row histogram and scan in shared memory write the
-//              bucket's row pointers, then each entry goes to its row's cursor
-// Entry order inside a row is arbitrary after this; the per-row sort of the
-// (col << 32 | entry index) keys gives the stable (row, col) order.
-constexpr int kBucketRows = 4096;
-constexpr int kMaxBuckets = 4096;              // rows up to 2^24 take this path
+//   partition  CTA c sorts its chunk by bucket in shared memory (counting sort,
+//              ranks from shared-memory atomics) and writes it out bucket by bucket,
+//              so each bucket receives one contiguous run per CTA: (row within the
+//              bucket, col << 32 | entry index, value)
+//   bucket     a CTA per bucket, all in shared memory: row histogram and scan (the
+//              row pointers), the entries of rows of up to kTiny entries placed by
+//              row, each such row sorted by key in one thread's registers with its
+//              values, and the sorted bucket written out in order; entries of longer
+//              rows go to their row's place in a key buffer for the warp / CTA sorts
+// Entry order inside a row is arbitrary before the per-row sort of the
+// (col << 32 | entry index) keys, which gives the stable (row, col) order.
+constexpr int kBucketRows = 2048;
+constexpr int kMaxBuckets = 4096;              // rows up to 2^23 take this path
 constexpr int kPartChunk = 8192;               // entries per CTA in the count / partition passes
 constexpr int64_t kMaxCountCells = 1ll << 24;  // cells of the count matrix (the chunk grows past it)
+constexpr int kTiny = 8;                       // rows of up to kTiny entries sort in one thread's registers
+constexpr int kPartThreads = 1024;
+constexpr int kBucketThreads = 1024;
+constexpr int kMaxSub = 64;  // sub-ranges per bucket: kBucketRows * kTiny / (cap - kTiny) at most
 
 __host__ __device__ inline int64_t coo_chunk(int64_t nnz, int nb) {
   const int64_t per = kMaxCountCells / nb;  // CTAs the matrix can hold
@@ -404,6 +413,13 @@ __host__ __device__ inline int64_t coo_chunk(int64_t nnz, int nb) {
 __device__ __forceinline__ bool coo_ok(long long r, long long c, int64_t m, int64_t n) {
   return r >= 0 && r < m && c >= 0 && c < n;
 }
+
+// value payload carried through the partition (ESZ 0: none; the emitted "value" is the
+// entry index, which the key holds)
+template <int ESZ> struct CooVal { using type = unsigned long long; };
+template <> struct CooVal<4> { using type = uint32_t; };
+template <> struct CooVal<2> { using type = uint16_t; };
+template <> struct CooVal<0> { using type = uint8_t; };
 
 __global__ void __launch_bounds__(256) coo_bucket_count_kernel(int64_t nnz, int64_t m, int64_t n, int nb,
                                                                int64_t chunk, const long long* __restrict__ rows,
@@ -435,99 +451,277 @@ __global__ void __launch_bounds__(256) coo_bucket_count_kernel(int64_t nnz, int6
   for (int b = threadIdx.x; b < nb; b += blockDim.x) cm[1 + b * G + c] = cnt[b];
 }
 
-__global__ void __launch_bounds__(256) coo_partition_kernel(int64_t nnz, int64_t m, int64_t n, int nb, int64_t chunk,
-                                                            const long long* __restrict__ rows,
-                                                            const long long* __restrict__ cols,
-                                                            const long long* __restrict__ cm,
-                                                            int* __restrict__ prow,
-                                                            unsigned long long* __restrict__ pkey) {
-  __shared__ int cnt[kMaxBuckets];
-  __shared__ long long base[kMaxBuckets];
-  const int64_t G = gridDim.x, c = blockIdx.x;
-  const int64_t c0 = c * chunk, c1 = c0 + chunk < nnz ? c0 + chunk : nnz;
-  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-    cnt[b] = 0;
-    base[b] = cm[b * G + c];
+// Exclusive scan of n <= per * blockDim.x ints in place (per consecutive values a thread).
+template <int PER>
+__device__ __forceinline__ void block_excl_scan_ints(unsigned* v, int n, long long* warp_tot) {
+  unsigned loc[PER], t = 0;
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x * PER + q;
+    loc[q] = i < n ? v[i] : 0u;
+    t += loc[q];
   }
-  __syncthreads();
-  for (int64_t e0 = c0 + threadIdx.x; e0 < c1; e0 += 4 * blockDim.x) {
-    long long r[4], k[4];
+  const long long inc = block_scan_incl(t, warp_tot, nullptr);
+  unsigned off = static_cast<unsigned>(inc) - t;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t e = e0 + u * blockDim.x;
-      r[u] = e < c1 ? rows[e] : -1;
-      k[u] = e < c1 ? cols[e] : -1;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (!coo_ok(r[u], k[u], m, n)) continue;
-      const int b = static_cast<int>(r[u] / kBucketRows);
-      const long long p = base[b] + atomicAdd(&cnt[b], 1);
-      prow[p] = static_cast<int>(r[u] - static_cast<long long>(b) * kBucketRows);
-      pkey[p] = (static_cast<unsigned long long>(k[u]) << 32) |
-                static_cast<unsigned long long>(e0 + u * blockDim.x);
-    }
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x * PER + q;
+    if (i < n) v[i] = off;
+    off += loc[q];
   }
 }
 
-// bucket b's entries: [cm[b * G], cm[(b + 1) * G]) (the last bound is cm[nb * G], the total)
-__global__ void __launch_bounds__(256) coo_bucket_rows_kernel(int64_t m, int nb, int64_t G,
-                                                              const long long* __restrict__ cm,
-                                                              const int* __restrict__ prow,
-                                                              const unsigned long long* __restrict__ pkey,
-                                                              long long* __restrict__ row_ptr,
-                                                              unsigned long long* __restrict__ keys) {
-  __shared__ unsigned int cur[kBucketRows];
-  __shared__ unsigned int wsum[8];
-  constexpr int kPer = kBucketRows / 256;  // bins per thread in the scan
+size_t coo_partition_smem(int esz) {
+  return 4 * sizeof(unsigned) * kMaxBuckets +
+         static_cast<size_t>(kPartChunk) * (sizeof(unsigned long long) + (esz ? esz : 1) + 2 * sizeof(uint16_t));
+}
+
+// The CTA's chunk in sub-tiles of kPartChunk entries, kPartPer per thread held in
+// registers (all loads of a thread in flight together): count per bucket, scan, place
+// each entry at its bucket's place in shared memory, then write the sub-tile out in
+// bucket order (each bucket's entries continue where the previous sub-tile's stopped).
+template <int ESZ>
+__global__ void __launch_bounds__(kPartThreads) coo_partition_kernel(
+    int64_t nnz, int64_t m, int64_t n, int nb, int64_t chunk, const long long* __restrict__ rows,
+    const long long* __restrict__ cols, const void* __restrict__ vals, const long long* __restrict__ cm,
+    uint16_t* __restrict__ plrow, unsigned long long* __restrict__ pkey, void* __restrict__ pval) {
+  using V = typename CooVal<ESZ>::type;
+  constexpr int kPer = kPartChunk / kPartThreads;
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ long long warp_tot[32];
+  unsigned* cnt = reinterpret_cast<unsigned*>(sm);  // per bucket: count in this sub-tile
+  unsigned* lst = cnt + kMaxBuckets;                // its start in the staged sub-tile
+  unsigned* cur = lst + kMaxBuckets;                // placement cursor
+  unsigned* gb = cur + kMaxBuckets;                 // next output position (nnz < 2^32)
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(gb + kMaxBuckets);
+  uint16_t* slr = reinterpret_cast<uint16_t*>(skey + kPartChunk);
+  uint16_t* sbk = slr + kPartChunk;
+  V* sval = reinterpret_cast<V*>(sbk + kPartChunk);
+  const V* vin = static_cast<const V*>(vals);
+  V* vout = static_cast<V*>(pval);
+  const int64_t G = gridDim.x, c = blockIdx.x;
+  const int64_t c0 = c * chunk, c1 = c0 + chunk < nnz ? c0 + chunk : nnz;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) gb[b] = static_cast<unsigned>(cm[b * G + c]);
+  for (int64_t t0 = c0; t0 < c1; t0 += kPartChunk) {
+    long long r[kPer], k[kPer];
+    V v[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int64_t e = t0 + threadIdx.x + u * kPartThreads;
+      r[u] = e < c1 ? rows[e] : -1;
+      k[u] = e < c1 ? cols[e] : -1;
+      if constexpr (ESZ > 0) v[u] = e < c1 ? vin[e] : V(0);
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+      cnt[b] = 0;
+      cur[b] = 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kPer; ++u)
+      if (coo_ok(r[u], k[u], m, n)) atomicAdd(&cnt[r[u] / kBucketRows], 1u);
+    __syncthreads();
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) lst[b] = cnt[b];
+    __syncthreads();
+    block_excl_scan_ints<kMaxBuckets / kPartThreads>(lst, nb, warp_tot);
+    __syncthreads();
+    const int np = static_cast<int>(lst[nb - 1] + cnt[nb - 1]);
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      if (!coo_ok(r[u], k[u], m, n)) continue;
+      const int b = static_cast<int>(r[u] / kBucketRows);
+      const unsigned slot = lst[b] + atomicAdd(&cur[b], 1u);
+      skey[slot] = (static_cast<unsigned long long>(k[u]) << 32) |
+                   static_cast<unsigned long long>(t0 + threadIdx.x + u * kPartThreads);
+      slr[slot] = static_cast<uint16_t>(r[u] - static_cast<long long>(b) * kBucketRows);
+      sbk[slot] = static_cast<uint16_t>(b);
+      if constexpr (ESZ > 0) sval[slot] = v[u];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < np; i += blockDim.x) {
+      const int b = sbk[i];
+      const size_t pos = static_cast<size_t>(gb[b]) + (i - lst[b]);
+      plrow[pos] = slr[i];
+      pkey[pos] = skey[i];
+      if constexpr (ESZ > 0) vout[pos] = sval[i];
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) gb[b] += cnt[b];
+  }
+}
+
+size_t coo_bucket_smem_fixed() { return 5 * sizeof(int) * kBucketRows; }
+int coo_bucket_entry_bytes(int esz) {
+  return static_cast<int>(sizeof(unsigned long long) + sizeof(uint16_t) + (esz ? esz : 1));
+}
+
+// A CTA per bucket (persistent over buckets). cap: entries the staging area holds.
+// Rows of up to kTiny entries are staged by row (in sub-ranges of at most cap - kTiny
+// entries when the bucket's short rows hold more than that), sorted in registers,
+// written back in place and then copied out in order; longer rows go to `keys` at
+// their row's place and are listed for the warp / CTA sorts.
+template <int ESZ>
+__global__ void __launch_bounds__(kBucketThreads) coo_bucket_sort_kernel(
+    int64_t m, int nb, int64_t G, int cap, const long long* __restrict__ cm, const uint16_t* __restrict__ plrow,
+    const unsigned long long* __restrict__ pkey, const void* __restrict__ pval, long long* __restrict__ row_ptr,
+    unsigned long long* __restrict__ keys, long long* __restrict__ cols_out, void* __restrict__ vals_out,
+    long long* __restrict__ mid_rows, unsigned long long* __restrict__ n_mid, long long* __restrict__ long_rows,
+    unsigned long long* __restrict__ n_long) {
+  using V = typename CooVal<ESZ>::type;
+  constexpr int kPer = kBucketRows / kBucketThreads;
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ long long warp_tot[32];
+  __shared__ long long tiny_total;
+  __shared__ int bnd[kMaxSub + 1];
+  int* cnt = reinterpret_cast<int*>(sm);  // entries per row
+  int* rst = cnt + kBucketRows;           // row start in the bucket (all rows)
+  int* tst = rst + kBucketRows;           // start among the short rows' entries
+  int* curT = tst + kBucketRows;
+  int* curL = curT + kBucketRows;
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(curL + kBucketRows);
+  uint16_t* srow = reinterpret_cast<uint16_t*>(skey + cap);
+  V* sval = reinterpret_cast<V*>(srow + cap);
+  const V* vin = static_cast<const V*>(pval);
+  const int capE = cap - kTiny;
   for (int b = blockIdx.x; b < nb; b += gridDim.x) {
     const int64_t r0 = static_cast<int64_t>(b) * kBucketRows;
     const int nr = static_cast<int>(m - r0 < kBucketRows ? m - r0 : kBucketRows);
     const long long s = cm[b * G], e = cm[(b + 1) * G];
-    const unsigned int len = static_cast<unsigned int>(e - s);
+    const int len = static_cast<int>(e - s);
     __syncthreads();
-    for (int i = threadIdx.x; i < kBucketRows; i += blockDim.x) cur[i] = 0;
+    for (int i = threadIdx.x; i < kBucketRows; i += blockDim.x) {
+      cnt[i] = 0;
+      curT[i] = 0;
+      curL[i] = 0;
+    }
     __syncthreads();
-    for (unsigned int i = threadIdx.x; i < len; i += blockDim.x) atomicAdd(&cur[prow[s + i]], 1u);
+    for (int i0 = threadIdx.x; i0 < len; i0 += 4 * kBucketThreads) {
+      int lr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) lr[u] = i0 + u * kBucketThreads < len ? plrow[s + i0 + u * kBucketThreads] : -1;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (lr[u] >= 0) atomicAdd(&cnt[lr[u]], 1);
+    }
     __syncthreads();
-    unsigned int v[kPer], tot = 0;
+    // row starts (all rows) and starts among the short rows' entries
+    int cv[kPer], ta = 0, tt = 0;
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      v[q] = cur[threadIdx.x * kPer + q];
-      tot += v[q];
+      cv[q] = cnt[threadIdx.x * kPer + q];
+      ta += cv[q];
+      tt += cv[q] <= kTiny ? cv[q] : 0;
     }
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    unsigned int inc = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned int y = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += y;
-    }
-    if (lane == 31) wsum[w] = inc;
-    __syncthreads();
-    unsigned int off = inc - tot;
-    for (int k = 0; k < w; ++k) off += wsum[k];
+    const long long ia = block_scan_incl(ta, warp_tot, nullptr);
+    __syncthreads();  // warp_tot is reused
+    long long tt_total = 0;
+    const long long it = block_scan_incl(tt, warp_tot, &tt_total);
+    int oa = static_cast<int>(ia) - ta, ot = static_cast<int>(it) - tt;
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
       const int i = threadIdx.x * kPer + q;
-      cur[i] = off;
-      if (i < nr) row_ptr[r0 + i] = s + off;
-      off += v[q];
+      rst[i] = oa;
+      tst[i] = ot;
+      if (i < nr) {
+        row_ptr[r0 + i] = s + oa;
+        if (cv[q] > 32) long_rows[atomicAdd(n_long, 1ull)] = r0 + i;
+        else if (cv[q] > kTiny) mid_rows[atomicAdd(n_mid, 1ull)] = r0 + i;
+      }
+      oa += cv[q];
+      ot += cv[q] <= kTiny ? cv[q] : 0;
     }
+    if (threadIdx.x == 0) tiny_total = tt_total;
     if (r0 + nr == m && threadIdx.x == 0) row_ptr[m] = e;
     __syncthreads();
-    for (unsigned int i0 = threadIdx.x; i0 < len; i0 += 4u * blockDim.x) {
-      int rr[4];
-      unsigned long long kk[4];
+    const int T = static_cast<int>(tiny_total);
+    const int nsub = T > 0 ? (T + capE - 1) / capE : 1;
+    // bnd[k]: the start (among the short rows' entries) of sub-range k's first row; every
+    // window of capE >= kTiny entries holds a row start, so no sub-range is empty
+    for (int k = threadIdx.x; k <= nsub; k += blockDim.x) bnd[k] = T;
+    __syncthreads();
+    for (int r = threadIdx.x; r < nr; r += blockDim.x)
+      if (cnt[r] > 0 && cnt[r] <= kTiny) atomicMin(&bnd[tst[r] / capE], tst[r]);
+    __syncthreads();
+    for (int k = 0; k < nsub; ++k) {
+      const int sb = k * capE;
+      for (int i0 = threadIdx.x; i0 < len; i0 += 4 * kBucketThreads) {
+        int lr[4];
+        unsigned long long kk[4];
+        V vv[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const unsigned int i = i0 + u * blockDim.x;
-        rr[u] = i < len ? prow[s + i] : -1;
-        kk[u] = i < len ? pkey[s + i] : 0ull;
+        for (int u = 0; u < 4; ++u) {
+          const int i = i0 + u * kBucketThreads;
+          lr[u] = i < len ? plrow[s + i] : -1;
+          kk[u] = i < len ? pkey[s + i] : 0ull;
+          if constexpr (ESZ > 0) vv[u] = i < len ? vin[s + i] : V(0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (lr[u] < 0) continue;
+          const int cn = cnt[lr[u]];
+          if (cn <= kTiny) {
+            if (tst[lr[u]] / capE != k) continue;
+            const int slot = tst[lr[u]] - sb + atomicAdd(&curT[lr[u]], 1);
+            skey[slot] = kk[u];
+            srow[slot] = static_cast<uint16_t>(lr[u]);
+            if constexpr (ESZ > 0) sval[slot] = vv[u];
+          } else if (k == 0) {
+            keys[s + rst[lr[u]] + atomicAdd(&curL[lr[u]], 1)] = kk[u];
+          }
+        }
       }
+      __syncthreads();
+      // sort each short row of this sub-range in registers (values follow their keys)
+      for (int r = threadIdx.x; r < nr; r += blockDim.x) {
+        const int cn = cnt[r];
+        if (cn == 0 || cn > kTiny || tst[r] / capE != k) continue;
+        const int base = tst[r] - sb;
+        unsigned long long kk[kTiny];
+        V vv[kTiny];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (rr[u] >= 0) keys[s + atomicAdd(&cur[rr[u]], 1u)] = kk[u];
+        for (int i = 0; i < kTiny; ++i) {
+          kk[i] = i < cn ? skey[base + i] : ~0ull;
+          if constexpr (ESZ > 0) vv[i] = i < cn ? sval[base + i] : V(0);
+        }
+#pragma unroll
+        for (int i = 0; i < kTiny - 1; ++i) {
+#pragma unroll
+          for (int j = 0; j < kTiny - 1 - i; ++j) {
+            const bool sw = kk[j + 1] < kk[j];
+            const unsigned long long a = kk[j], c2 = kk[j + 1];
+            kk[j] = sw ? c2 : a;
+            kk[j + 1] = sw ? a : c2;
+            if constexpr (ESZ > 0) {
+              const V va = vv[j], vc = vv[j + 1];
+              vv[j] = sw ? vc : va;
+              vv[j + 1] = sw ? va : vc;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kTiny; ++i) {
+          if (i < cn) {
+            skey[base + i] = kk[i];
+            if constexpr (ESZ > 0) sval[base + i] = vv[i];
+          }
+        }
+      }
+      __syncthreads();
+      // copy the sorted sub-range out in order: its staged slots are contiguous, from its
+      // first row's start to the next sub-range's first row's start
+      const int lo = bnd[k] - sb, hi = bnd[k + 1] - sb;
+      for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const int r = srow[i];
+        const long long out = s + rst[r] + (i - (tst[r] - sb));
+        const unsigned long long key = skey[i];
+        cols_out[out] = static_cast<long long>(key >> 32);
+        if constexpr (ESZ > 0)
+          static_cast<V*>(vals_out)[out] = sval[i];
+        else
+          static_cast<long long*>(vals_out)[out] = static_cast<long long>(key & 0xffffffffull);
+      }
+      __syncthreads();
     }
   }
 }
@@ -546,8 +740,6 @@ __device__ __forceinline__ void coo_emit(unsigned long long key, long long p, co
   else
     reinterpret_cast<uint64_t*>(vals_out)[p] = reinterpret_cast<const uint64_t*>(vals_in)[src];
 }
-
-constexpr int kTiny = 8;  // rows of up to kTiny entries sort in one thread's registers
 
 // A thread per row: rows of at most kTiny entries are sorted in registers (an unrolled
 // exchange network); longer rows are listed for the warp (<= 32) or CTA passes.
@@ -905,16 +1097,72 @@ extern "C" int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A
 }
 
 // ---------------------------------------------------------------- COO -> CSR
+namespace tsb {
+namespace {
+template <int ESZ>
+int coo_bucketed_launch(int64_t m, int64_t n, int64_t nnz, int nb, int64_t chunk, int64_t G, const long long* rows,
+                        const long long* cols, const void* values, const long long* cm, uint16_t* plrow,
+                        unsigned long long* pkey, void* pval, long long* row_ptr, unsigned long long* keys,
+                        long long* cols_out, void* values_out, long long* mid_rows, unsigned long long* n_mid,
+                        long long* long_rows, unsigned long long* n_long, cudaStream_t st) {
+  if (nnz > 0) {
+    auto pk = coo_partition_kernel<ESZ>;
+    const size_t psm = coo_partition_smem(ESZ);
+    cudaError_t e = cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm);
+    if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: partition smem");
+    pk<<<(unsigned)G, kPartThreads, psm, st>>>(nnz, m, n, nb, chunk, rows, cols, values, cm, plrow, pkey, pval);
+    TSB_CHECK_LAUNCH("coo_to_csr: partition");
+  }
+  auto bk = coo_bucket_sort_kernel<ESZ>;
+  const size_t budget = 200 * 1024;
+  const int cap = static_cast<int>((budget - coo_bucket_smem_fixed()) / coo_bucket_entry_bytes(ESZ)) & ~7;
+  const size_t bsm = coo_bucket_smem_fixed() + static_cast<size_t>(cap) * coo_bucket_entry_bytes(ESZ) + 16;
+  cudaError_t e = cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
+  if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: bucket smem");
+  const int grid = nb < sm_count() ? nb : sm_count();
+  bk<<<grid, kBucketThreads, bsm, st>>>(m, nb, G, cap, cm, plrow, pkey, pval, row_ptr, keys, cols_out, values_out,
+                                        mid_rows, n_mid, long_rows, n_long);
+  TSB_CHECK_LAUNCH("coo_to_csr: bucket sort");
+  return TRNSPARSE_OK;
+}
+
+// esz: value bytes (2, 4 or 8), or 0 with values == nullptr (emit the entry index)
+int coo_bucketed_sort(int esz, int64_t m, int64_t n, int64_t nnz, int nb, int64_t chunk, int64_t G,
+                      const long long* rows, const long long* cols, const void* values, const long long* cm,
+                      uint16_t* plrow, unsigned long long* pkey, void* pval, long long* row_ptr,
+                      unsigned long long* keys, long long* cols_out, void* values_out, long long* mid_rows,
+                      unsigned long long* n_mid, long long* long_rows, unsigned long long* n_long, cudaStream_t st) {
+  if (values == nullptr) esz = 0;
+  switch (esz) {
+    case 0:
+      return coo_bucketed_launch<0>(m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, pkey, pval, row_ptr,
+                                    keys, cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+    case 2:
+      return coo_bucketed_launch<2>(m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, pkey, pval, row_ptr,
+                                    keys, cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+    case 4:
+      return coo_bucketed_launch<4>(m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, pkey, pval, row_ptr,
+                                    keys, cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+    default:
+      return coo_bucketed_launch<8>(m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, pkey, pval, row_ptr,
+                                    keys, cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+  }
+}
+}  // namespace
+}  // namespace tsb
+
 extern "C" size_t trnsparse_coo_to_csr_workspace_size(int64_t m, int64_t nnz) {
   if (m < 0 || nnz < 0) return 0;
   // keys, keys2, cursors, scan partials, row lists, counters; then, for the bucketed
-  // path, the local rows (int32 per entry), the count matrix and its scan partials
+  // path, the partitioned values (up to 8 bytes each), the local rows (16 bits per
+  // entry), the count matrix and its scan partials
   size_t extra = 0;
   if (m > 0 && m <= static_cast<int64_t>(kBucketRows) * kMaxBuckets) {
     const int nb = static_cast<int>((m + kBucketRows - 1) / kBucketRows);
     const int64_t chunk = coo_chunk(nnz, nb);
     const int64_t G = nnz > 0 ? (nnz + chunk - 1) / chunk : 1;
-    extra = sizeof(int) * (size_t)nnz + 16 + sizeof(long long) * (size_t)(nb * G + 1) + scan_ws_bytes(nb * G);
+    extra = 8 * (size_t)nnz + ((sizeof(uint16_t) * (size_t)nnz + 255) & ~(size_t)255) + 16 + sizeof(long long) * (size_t)(nb * G + 1) +
+            scan_ws_bytes(nb * G);
   }
   return sizeof(unsigned long long) * (size_t)(2 * nnz + 3 * m + 1) + scan_ws_bytes(m) + 32 + extra;
 }
@@ -946,9 +1194,10 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
     const int nb = static_cast<int>((m + kBucketRows - 1) / kBucketRows);
     const int64_t chunk = coo_chunk(nnz, nb);
     const int64_t G = nnz > 0 ? (nnz + chunk - 1) / chunk : 1;
-    int* prow = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(n_mid) + 32);  // past n_mid, n_long, bad
+    uint8_t* pval = reinterpret_cast<uint8_t*>(n_mid) + 32;  // past n_mid, n_long, bad (8 bytes per entry)
+    uint16_t* plrow = reinterpret_cast<uint16_t*>(pval + 8 * (size_t)nnz);
     long long* cm = reinterpret_cast<long long*>(
-        (reinterpret_cast<uintptr_t>(prow + nnz) + 15) & ~static_cast<uintptr_t>(15));  // nb * G + 1 cells
+        (reinterpret_cast<uintptr_t>(plrow + nnz) + 15) & ~static_cast<uintptr_t>(15));  // nb * G + 1 cells
     long long* cpart = cm + nb * G + 1;                                                   // its scan partials
     if (nnz > 0) {
       coo_bucket_count_kernel<<<(unsigned)G, 256, 0, st>>>(nnz, m, n, nb, chunk, rows, cols, cm, bad);
@@ -959,12 +1208,17 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
     }
     int rc = exclusive_scan(cm, nb * G, cpart, st);
     if (rc) return rc;
-    if (nnz > 0)
-      coo_partition_kernel<<<(unsigned)G, 256, 0, st>>>(nnz, m, n, nb, chunk, rows, cols, cm, prow, keys2);
-    coo_bucket_rows_kernel<<<(unsigned)(nb < 32 * sm_count() ? nb : 32 * sm_count()), 256, 0, st>>>(
-        m, nb, G, cm, prow, keys2, row_ptr, keys);
-    TSB_CHECK_LAUNCH("coo_to_csr: bucket rows");
+    rc = coo_bucketed_sort(esz, m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, keys2, pval, row_ptr, keys,
+                           cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+    if (rc) return rc;
     if (nnz == 0) return TRNSPARSE_OK;
+    // the rows of more than kTiny entries (listed by the bucket pass)
+    coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, (const uint8_t*)values,
+                                                       esz, cols_out, (uint8_t*)values_out);
+    coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(row_ptr, long_rows, n_long, keys, keys2,
+                                                                 (const uint8_t*)values, esz, cols_out,
+                                                                 (uint8_t*)values_out);
+    TSB_CHECK_LAUNCH("coo_to_csr: sort");
   } else {
     e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
     if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
@@ -979,15 +1233,15 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
     e = cudaMemcpyAsync(cursor, row_ptr, sizeof(long long) * m, cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: cursors");
     coo_scatter_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols, cursor, keys);
+    coo_sort_tiny_kernel<<<grid_for(m, 256), 256, 0, st>>>(m, row_ptr, keys, (const uint8_t*)values, esz, cols_out,
+                                                          (uint8_t*)values_out, mid_rows, n_mid, long_rows, n_long);
+    coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, (const uint8_t*)values, esz,
+                                                       cols_out, (uint8_t*)values_out);
+    coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(row_ptr, long_rows, n_long, keys, keys2,
+                                                                 (const uint8_t*)values, esz, cols_out,
+                                                                 (uint8_t*)values_out);
+    TSB_CHECK_LAUNCH("coo_to_csr: sort");
   }
-  coo_sort_tiny_kernel<<<grid_for(m, 256), 256, 0, st>>>(m, row_ptr, keys, (const uint8_t*)values, esz, cols_out,
-                                                        (uint8_t*)values_out, mid_rows, n_mid, long_rows, n_long);
-  coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, (const uint8_t*)values, esz,
-                                                     cols_out, (uint8_t*)values_out);
-  coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(row_ptr, long_rows, n_long, keys, keys2,
-                                                               (const uint8_t*)values, esz, cols_out,
-                                                               (uint8_t*)values_out);
-  TSB_CHECK_LAUNCH("coo_to_csr: sort");
   // an out-of-range index is an argument error the caller sees on the host
   int hbad = 0;
   e = cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, st);
