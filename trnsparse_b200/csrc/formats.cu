@@ -395,13 +395,28 @@ __global__ void coo_scatter_kernel(int64_t nnz, int64_t m, int64_t n, const long
 //              rows go to their row's place in a key buffer for the warp / CTA sorts
 // Entry order inside a row is arbitrary before the per-row sort of the
 // (col << 32 | entry index) keys, which gives the stable (row, col) order.
-constexpr int kBucketRows = 2048;
+#ifndef TSB_COO_BUCKET_ROWS
+#define TSB_COO_BUCKET_ROWS 2048
+#endif
+#ifndef TSB_COO_BUCKET_KB
+#define TSB_COO_BUCKET_KB 200
+#endif
+constexpr int kBucketRows = TSB_COO_BUCKET_ROWS;
 constexpr int kMaxBuckets = 4096;              // rows up to 2^23 take this path
-constexpr int kPartChunk = 8192;               // entries per CTA in the count / partition passes
+#ifndef TSB_COO_PART_CHUNK
+#define TSB_COO_PART_CHUNK 8192
+#endif
+#ifndef TSB_COO_PART_THREADS
+#define TSB_COO_PART_THREADS 1024
+#endif
+constexpr int kPartChunk = TSB_COO_PART_CHUNK;  // entries per CTA in the count / partition passes
 constexpr int64_t kMaxCountCells = 1ll << 24;  // cells of the count matrix (the chunk grows past it)
 constexpr int kTiny = 8;                       // rows of up to kTiny entries sort in one thread's registers
-constexpr int kPartThreads = 1024;
-constexpr int kBucketThreads = 1024;
+constexpr int kPartThreads = TSB_COO_PART_THREADS;
+#ifndef TSB_COO_BUCKET_THREADS
+#define TSB_COO_BUCKET_THREADS 1024
+#endif
+constexpr int kBucketThreads = TSB_COO_BUCKET_THREADS;
 constexpr int kMaxSub = 64;  // sub-ranges per bucket: kBucketRows * kTiny / (cap - kTiny) at most
 
 __host__ __device__ inline int64_t coo_chunk(int64_t nnz, int nb) {
@@ -471,8 +486,9 @@ __device__ __forceinline__ void block_excl_scan_ints(unsigned* v, int n, long lo
   }
 }
 
-size_t coo_partition_smem(int esz) {
-  return 4 * sizeof(unsigned) * kMaxBuckets +
+__host__ __device__ inline int coo_nb_pad(int nb) { return (nb + 3) & ~3; }
+size_t coo_partition_smem(int esz, int nb) {
+  return 4 * sizeof(unsigned) * coo_nb_pad(nb) +
          static_cast<size_t>(kPartChunk) * (sizeof(unsigned long long) + (esz ? esz : 1) + 2 * sizeof(uint16_t));
 }
 
@@ -489,11 +505,12 @@ __global__ void __launch_bounds__(kPartThreads) coo_partition_kernel(
   constexpr int kPer = kPartChunk / kPartThreads;
   extern __shared__ __align__(16) uint8_t sm[];
   __shared__ long long warp_tot[32];
+  const int nbp = coo_nb_pad(nb);
   unsigned* cnt = reinterpret_cast<unsigned*>(sm);  // per bucket: count in this sub-tile
-  unsigned* lst = cnt + kMaxBuckets;                // its start in the staged sub-tile
-  unsigned* cur = lst + kMaxBuckets;                // placement cursor
-  unsigned* gb = cur + kMaxBuckets;                 // next output position (nnz < 2^32)
-  unsigned long long* skey = reinterpret_cast<unsigned long long*>(gb + kMaxBuckets);
+  unsigned* lst = cnt + nbp;                        // its start in the staged sub-tile
+  unsigned* cur = lst + nbp;                        // placement cursor
+  unsigned* gb = cur + nbp;                         // next output position (nnz < 2^32)
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(gb + nbp);
   uint16_t* slr = reinterpret_cast<uint16_t*>(skey + kPartChunk);
   uint16_t* sbk = slr + kPartChunk;
   V* sval = reinterpret_cast<V*>(sbk + kPartChunk);
@@ -524,7 +541,7 @@ __global__ void __launch_bounds__(kPartThreads) coo_partition_kernel(
     __syncthreads();
     for (int b = threadIdx.x; b < nb; b += blockDim.x) lst[b] = cnt[b];
     __syncthreads();
-    block_excl_scan_ints<kMaxBuckets / kPartThreads>(lst, nb, warp_tot);
+    block_excl_scan_ints<(kMaxBuckets + kPartThreads - 1) / kPartThreads>(lst, nb, warp_tot);
     __syncthreads();
     const int np = static_cast<int>(lst[nb - 1] + cnt[nb - 1]);
 #pragma unroll
@@ -636,12 +653,13 @@ __global__ void __launch_bounds__(kBucketThreads) coo_bucket_sort_kernel(
     __syncthreads();
     const int T = static_cast<int>(tiny_total);
     const int nsub = T > 0 ? (T + capE - 1) / capE : 1;
+    auto sub_of = [&](int t) { return nsub == 1 ? 0 : t / capE; };
     // bnd[k]: the start (among the short rows' entries) of sub-range k's first row; every
     // window of capE >= kTiny entries holds a row start, so no sub-range is empty
     for (int k = threadIdx.x; k <= nsub; k += blockDim.x) bnd[k] = T;
     __syncthreads();
     for (int r = threadIdx.x; r < nr; r += blockDim.x)
-      if (cnt[r] > 0 && cnt[r] <= kTiny) atomicMin(&bnd[tst[r] / capE], tst[r]);
+      if (cnt[r] > 0 && cnt[r] <= kTiny) atomicMin(&bnd[sub_of(tst[r])], tst[r]);
     __syncthreads();
     for (int k = 0; k < nsub; ++k) {
       const int sb = k * capE;
@@ -661,7 +679,7 @@ __global__ void __launch_bounds__(kBucketThreads) coo_bucket_sort_kernel(
           if (lr[u] < 0) continue;
           const int cn = cnt[lr[u]];
           if (cn <= kTiny) {
-            if (tst[lr[u]] / capE != k) continue;
+            if (sub_of(tst[lr[u]]) != k) continue;
             const int slot = tst[lr[u]] - sb + atomicAdd(&curT[lr[u]], 1);
             skey[slot] = kk[u];
             srow[slot] = static_cast<uint16_t>(lr[u]);
@@ -675,7 +693,7 @@ __global__ void __launch_bounds__(kBucketThreads) coo_bucket_sort_kernel(
       // sort each short row of this sub-range in registers (values follow their keys)
       for (int r = threadIdx.x; r < nr; r += blockDim.x) {
         const int cn = cnt[r];
-        if (cn == 0 || cn > kTiny || tst[r] / capE != k) continue;
+        if (cn == 0 || cn > kTiny || sub_of(tst[r]) != k) continue;
         const int base = tst[r] - sb;
         unsigned long long kk[kTiny];
         V vv[kTiny];
@@ -1107,14 +1125,14 @@ int coo_bucketed_launch(int64_t m, int64_t n, int64_t nnz, int nb, int64_t chunk
                         long long* long_rows, unsigned long long* n_long, cudaStream_t st) {
   if (nnz > 0) {
     auto pk = coo_partition_kernel<ESZ>;
-    const size_t psm = coo_partition_smem(ESZ);
+    const size_t psm = coo_partition_smem(ESZ, nb);
     cudaError_t e = cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm);
     if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: partition smem");
     pk<<<(unsigned)G, kPartThreads, psm, st>>>(nnz, m, n, nb, chunk, rows, cols, values, cm, plrow, pkey, pval);
     TSB_CHECK_LAUNCH("coo_to_csr: partition");
   }
   auto bk = coo_bucket_sort_kernel<ESZ>;
-  const size_t budget = 200 * 1024;
+  const size_t budget = TSB_COO_BUCKET_KB * 1024;
   const int cap = static_cast<int>((budget - coo_bucket_smem_fixed()) / coo_bucket_entry_bytes(ESZ)) & ~7;
   const size_t bsm = coo_bucket_smem_fixed() + static_cast<size_t>(cap) * coo_bucket_entry_bytes(ESZ) + 16;
   cudaError_t e = cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
