@@ -133,6 +133,8 @@ screened_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant
       ScSeg g;
       int it = 0;
       bool ok = true;
+      // A and Q stream through once per N tile; B^T (hi, lo) is re-read by every row tile
+      const uint64_t stream_pol = l2_policy_evict_first(), keep_pol = l2_policy_evict_last();
       while (ok && wk.next(g)) {
         const int n0 = g.n_tile * BN;
         for (int kc = g.kb0 * 4; ok && kc < g.kb1 * 4; ++kc, ++it) {
@@ -141,10 +143,10 @@ screened_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant
           if (*abort_flag) { ok = false; break; }
           const int kx = kc * 32;  // K coordinate of the 32-wide chunk
           mbar_arrive_expect_tx(&Bs.full[s], mode == 2 ? Lay::kStage : Lay::kStage - Lay::kATile);
-          tma_load_2d(a_hi(s), &ta, kx, g.row_tile * 128, &Bs.full[s]);
-          if (mode == 2) tma_load_2d(a_lo(s), &tq, kx, g.row_tile * 128, &Bs.full[s]);
-          tma_load_2d(b_hi(s), &tb_hi, kx, n0, &Bs.full[s]);
-          tma_load_2d(b_lo(s), &tb_lo, kx, n0, &Bs.full[s]);
+          tma_load_2d_hint(a_hi(s), &ta, kx, g.row_tile * 128, &Bs.full[s], stream_pol);
+          if (mode == 2) tma_load_2d_hint(a_lo(s), &tq, kx, g.row_tile * 128, &Bs.full[s], stream_pol);
+          tma_load_2d_hint(b_hi(s), &tb_hi, kx, n0, &Bs.full[s], keep_pol);
+          tma_load_2d_hint(b_lo(s), &tb_lo, kx, n0, &Bs.full[s], keep_pol);
         }
       }
       if (!ok) {
