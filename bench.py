@@ -687,7 +687,8 @@ def run_format_extras(pk: dict) -> dict:
     ex["formats_csr_from_dense_8192_d0017"] = {
         "ms": round(ms, 3), "GB/s": round(nb / (ms * 1e-3) / 1e9, 1), "nnz": csr.nnz,
         "frac_of_hbm": round(nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 3),
-        "note": "count and fill passes both read A (second read not counted)"}
+        "note": "the count pass reads A and writes a kept-entry bit mask; the fill gathers the kept values "
+                "through it (its reads not counted); one host read of nnz"}
     del Ad, csr
     A2 = w.poisson2d_csr(2048)
     counts = (A2.row_ptrs[1:] - A2.row_ptrs[:-1]).long()

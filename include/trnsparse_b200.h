@@ -476,6 +476,19 @@ TRNSPARSE_API int trnsparse_csr_from_dense_count(int64_t m, int64_t n, const voi
 TRNSPARSE_API int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
                                   float threshold, const long long* row_ptr, void* values, long long* col_idx,
                                   void* stream);
+/* The same count, also writing a bit mask of the kept entries (uint32 words,
+ * trnsparse_csr_from_dense_mask_bytes(m, n) bytes: bit c % 32 of word
+ * r * ceil(n / 32) + c / 32 for entry (r, c)); _fill_masked then gathers only
+ * the kept values instead of reading every row again (fewer bytes while the
+ * density stays below roughly one entry in eight 32-byte sectors). Same
+ * output as _fill. */
+TRNSPARSE_API size_t trnsparse_csr_from_dense_mask_bytes(int64_t m, int64_t n);
+TRNSPARSE_API int trnsparse_csr_from_dense_count_mask(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                        float threshold, long long* row_ptr, uint32_t* mask, void* ws,
+                                        size_t ws_bytes, void* stream);
+TRNSPARSE_API int trnsparse_csr_from_dense_fill_masked(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                         const long long* row_ptr, const uint32_t* mask, void* values,
+                                         long long* col_idx, void* stream);
 /* COOMatrix.to_csr (formats.py:104-124): entries ordered by (row, col),
  * entries with equal (row, col) in input order (a stable sort). rows, cols:
  * int64 device arrays of nnz entries (nnz < 2^32, n < 2^31); values of dtype

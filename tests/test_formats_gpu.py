@@ -67,24 +67,30 @@ def test_bsr_from_dense_device_edge_cases():
     assert ts._lib.device_error() == 0
 
 
-@pytest.mark.parametrize("m,n,thr,dtype", [
-    (1000, 700, 0.0, torch.float32),
-    (333, 4099, 0.5, torch.float32),
-    (64, 64, 0.1, torch.bfloat16),
-    (1, 100000, 1.0, torch.float32),
+@pytest.mark.parametrize("m,n,thr,dtype,zero_frac,offset", [
+    (1000, 700, 0.0, torch.float32, 0.7, 0),
+    (333, 4099, 0.5, torch.float32, 0.7, 0),
+    (64, 64, 0.1, torch.bfloat16, 0.7, 0),
+    (1, 100000, 1.0, torch.float32, 0.7, 0),
+    # sparse results take the masked fill (the count pass's bit mask, gathered values)
+    (777, 3001, 0.0, torch.float32, 0.98, 0),
+    (300, 1000, 0.0, torch.bfloat16, 0.99, 0),
+    (257, 999, 0.2, torch.float32, 0.98, 1),  # rows not 16-byte aligned: one element per lane
 ])
-def test_csr_from_dense_device_matches_host(m, n, thr, dtype):
+def test_csr_from_dense_device_matches_host(m, n, thr, dtype, zero_frac, offset):
     g = torch.Generator().manual_seed(m * 7 + n)
-    A = torch.randn(m, n, generator=g)
-    A[torch.rand(m, n, generator=g) < 0.7] = 0.0
+    A = torch.randn(m, n + offset, generator=g)
+    A[torch.rand(m, n + offset, generator=g) < zero_frac] = 0.0
     A[0, 0] = float("nan")
     A[m // 2, n // 3] = float("inf")
     A[m - 1, n - 1] = 0.1
     if m > 10:
         A[5] = 0.0  # an empty row
     A = A.to(dtype)
-    c = ts.from_dense(A.cuda(), threshold=thr)
-    vals, cols, ptrs = oracle.csr_from_dense(A, threshold=thr)
+    Ad = A.cuda()[:, offset:]
+    A = A[:, offset:]
+    c = ts.from_dense(Ad, threshold=thr)
+    vals, cols, ptrs = oracle.csr_from_dense(A.contiguous(), threshold=thr)
     assert c.values.is_cuda and c.row_ptrs.dtype == torch.int64 and c.col_indices.dtype == torch.int64
     assert torch.equal(c.row_ptrs.cpu(), ptrs)
     assert torch.equal(c.col_indices.cpu(), cols)

@@ -67,6 +67,9 @@ SIGNATURES.update({
     "trnsparse_csr_from_dense_workspace_size": [_i64],
     "trnsparse_csr_from_dense_count": [_i64, _i64, _p, _i64, _i32, C.c_float, _p, _p, _sz, _p],
     "trnsparse_csr_from_dense_fill": [_i64, _i64, _p, _i64, _i32, C.c_float, _p, _p, _p, _p],
+    "trnsparse_csr_from_dense_mask_bytes": [_i64, _i64],
+    "trnsparse_csr_from_dense_count_mask": [_i64, _i64, _p, _i64, _i32, C.c_float, _p, _p, _p, _sz, _p],
+    "trnsparse_csr_from_dense_fill_masked": [_i64, _i64, _p, _i64, _i32, _p, _p, _p, _p, _p],
     "trnsparse_coo_to_csr_workspace_size": [_i64, _i64],
     "trnsparse_coo_to_csr": [_i64, _i64, _i64, _p, _p, _p, _i32, _p, _p, _p, _p, _sz, _p],
     "trnsparse_bsr_attention_backward_tc": [_i64, _i64, _i64, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _p, _p,
@@ -116,6 +119,7 @@ _RESTYPE = {
     "trnsparse_bsr_attention_backward_tc_workspace_size": C.c_size_t,
     "trnsparse_bsr_from_dense_workspace_size": C.c_size_t,
     "trnsparse_csr_from_dense_workspace_size": C.c_size_t,
+    "trnsparse_csr_from_dense_mask_bytes": C.c_size_t,
     "trnsparse_coo_to_csr_workspace_size": C.c_size_t,
     "trnsparse_csr_transpose_workspace_size": C.c_size_t,
     "trnsparse_nt_tc_workspace_size": C.c_size_t,

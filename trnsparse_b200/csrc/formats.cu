@@ -291,6 +291,94 @@ __global__ void csr_count_kernel(int64_t m, int64_t n, const T* __restrict__ A, 
   }
 }
 
+// The count pass that also writes a bit mask of the kept entries (bit c % 32 of word
+// r * mw + c / 32 for entry (r, c)), so a fill can gather the kept values instead of
+// reading the rows again. All lanes walk every piece together (the mask words are
+// assembled across lanes).
+template <typename T, int VEC>
+__global__ void csr_count_mask_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda, float thr,
+                                      long long* __restrict__ v, uint32_t* __restrict__ mask, int64_t mw) {
+  constexpr int L = 32 / VEC;  // lanes per 32-bit mask word
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const T* row = A + r * lda;
+    uint32_t* mrow = mask + r * mw;
+    long long c = 0;
+    constexpr int kU = 4;  // pieces per batch: their loads are all in flight before any shuffle
+    for (int64_t jb = 0; jb < n; jb += kU * 32 * VEC) {
+      Vec<T, VEC> x[kU];
+      int cnt[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t j = jb + u * 32 * VEC + lane * VEC;
+        cnt[u] = 0;
+        if (j < n) x[u] = load_piece<T, VEC>(row, j, n, cnt[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t j0 = jb + u * 32 * VEC;
+        if (j0 >= n) break;  // uniform across the warp
+        unsigned bits = 0;
+#pragma unroll
+        for (int k = 0; k < VEC; ++k)
+          if (k < cnt[u] && fm_abs<T>(x[u].v[k]) > thr) bits |= 1u << k;
+        c += __popc(bits);
+        unsigned word;
+        if constexpr (VEC == 1) {
+          word = __ballot_sync(0xffffffffu, bits != 0);
+        } else {
+          word = bits << ((lane % L) * VEC);
+#pragma unroll
+          for (int o = 1; o < L; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+        }
+        const int64_t widx = j0 / 32 + lane / L;
+        if (lane % L == 0 && widx < mw) mrow[widx] = word;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == 0) v[1 + r] = c;
+  }
+}
+
+// Fill from the mask: a warp per row, lane l takes mask word w0 + l, a warp prefix sum of
+// the words' bit counts gives each lane its output offset, and the lane gathers its kept
+// entries in column order.
+template <typename T>
+__global__ void csr_fill_masked_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda,
+                                       const long long* __restrict__ row_ptr, const uint32_t* __restrict__ mask,
+                                       int64_t mw, T* __restrict__ vals, long long* __restrict__ cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const T* row = A + r * lda;
+    const uint32_t* mrow = mask + r * mw;
+    long long o = row_ptr[r];
+    for (int64_t w0 = 0; w0 < mw; w0 += 32) {
+      const int64_t w = w0 + lane;
+      unsigned bits = w < mw ? mrow[w] : 0u;
+      const int mine = __popc(bits);
+      int inc = mine;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += y;
+      }
+      long long p = o + inc - mine;
+      while (bits) {
+        const int b = __ffs(bits) - 1;
+        bits &= bits - 1;
+        const int64_t col = w * 32 + b;
+        vals[p] = row[col];
+        cols[p] = col;
+        ++p;
+      }
+      o += __shfl_sync(0xffffffffu, inc, 31);
+    }
+  }
+}
+
 template <typename T, int VEC>
 __global__ void csr_fill_kernel(int64_t m, int64_t n, const T* __restrict__ A, int64_t lda, float thr,
                                 const long long* __restrict__ row_ptr, T* __restrict__ vals,
@@ -1111,6 +1199,62 @@ extern "C" int trnsparse_csr_from_dense_fill(int64_t m, int64_t n, const void* A
       csr_fill_kernel<B16, 1><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr, (B16*)values, col_idx);
   }
   TSB_CHECK_LAUNCH("csr_from_dense: fill");
+  return TRNSPARSE_OK;
+}
+
+extern "C" size_t trnsparse_csr_from_dense_mask_bytes(int64_t m, int64_t n) {
+  return (m < 0 || n < 0) ? 0 : sizeof(uint32_t) * static_cast<size_t>(m) * static_cast<size_t>((n + 31) / 32);
+}
+
+extern "C" int trnsparse_csr_from_dense_count_mask(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                                   float threshold, long long* row_ptr, uint32_t* mask, void* ws,
+                                                   size_t ws_bytes, void* stream) {
+  TSB_REQUIRE(m >= 0 && n >= 0 && lda >= n, "csr_from_dense: bad sizes");
+  TSB_REQUIRE(dtype == TRNSPARSE_F32 || dtype == TRNSPARSE_BF16, "csr_from_dense: dtype must be F32 or BF16");
+  TSB_REQUIRE(row_ptr && ws && (A || m * n == 0) && (mask || m * n == 0), "csr_from_dense: null pointer");
+  TSB_REQUIRE(ws_bytes >= trnsparse_csr_from_dense_workspace_size(m), "csr_from_dense: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  if (m > 0) {
+    if (n == 0) {
+      cudaError_t e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
+      return cuda_status(e, "csr_from_dense: empty rows");
+    }
+    const int64_t mw = (n + 31) / 32;
+    const unsigned gr = grid_for(m, 8);
+    if (dtype == TRNSPARSE_F32) {
+      if (vec_ok(A, lda, 4, 4))
+        csr_count_mask_kernel<float, 4><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr, mask, mw);
+      else
+        csr_count_mask_kernel<float, 1><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, threshold, row_ptr, mask, mw);
+    } else {
+      using B16 = __nv_bfloat16;
+      if (vec_ok(A, lda, 8, 8))
+        csr_count_mask_kernel<B16, 8><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr, mask, mw);
+      else
+        csr_count_mask_kernel<B16, 1><<<gr, 256, 0, st>>>(m, n, (const B16*)A, lda, threshold, row_ptr, mask, mw);
+    }
+    TSB_CHECK_LAUNCH("csr_from_dense: count + mask");
+  }
+  return exclusive_scan(row_ptr, m, static_cast<long long*>(ws), st);
+}
+
+extern "C" int trnsparse_csr_from_dense_fill_masked(int64_t m, int64_t n, const void* A, int64_t lda, int dtype,
+                                                    const long long* row_ptr, const uint32_t* mask, void* values,
+                                                    long long* col_idx, void* stream) {
+  TSB_REQUIRE(m >= 0 && n >= 0 && lda >= n, "csr_from_dense: bad sizes");
+  TSB_REQUIRE(dtype == TRNSPARSE_F32 || dtype == TRNSPARSE_BF16, "csr_from_dense: dtype must be F32 or BF16");
+  if (m == 0 || n == 0) return TRNSPARSE_OK;
+  TSB_REQUIRE(A && row_ptr && mask && values && col_idx, "csr_from_dense: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const unsigned gr = grid_for(m, 8);
+  const int64_t mw = (n + 31) / 32;
+  if (dtype == TRNSPARSE_F32)
+    csr_fill_masked_kernel<float><<<gr, 256, 0, st>>>(m, n, (const float*)A, lda, row_ptr, mask, mw, (float*)values,
+                                                      col_idx);
+  else
+    csr_fill_masked_kernel<__nv_bfloat16><<<gr, 256, 0, st>>>(m, n, (const __nv_bfloat16*)A, lda, row_ptr, mask, mw,
+                                                              (__nv_bfloat16*)values, col_idx);
+  TSB_CHECK_LAUNCH("csr_from_dense: masked fill");
   return TRNSPARSE_OK;
 }
 

@@ -361,16 +361,25 @@ def _csr_from_dense_device(A: torch.Tensor, threshold: float) -> CSRMatrix:
     row_ptrs = torch.empty(m + 1, dtype=torch.int64, device=dev)
     ws_bytes = _lib.raw("trnsparse_csr_from_dense_workspace_size")(m)
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    # the count pass also writes a bit mask of the kept entries (1/32 of A's elements), so
+    # a sparse result is gathered through it instead of reading A a second time
+    mask = torch.empty(max(_lib.raw("trnsparse_csr_from_dense_mask_bytes")(m, n) // 4, 1), dtype=torch.int32,
+                       device=dev)
     with torch.cuda.device(dev):
         st = _lib.stream_handle(dev)
-        _lib.call("trnsparse_csr_from_dense_count", m, n, A.data_ptr(), lda, code, thr, row_ptrs.data_ptr(),
-                  ws.data_ptr(), ws_bytes, st)
+        _lib.call("trnsparse_csr_from_dense_count_mask", m, n, A.data_ptr(), lda, code, thr, row_ptrs.data_ptr(),
+                  mask.data_ptr(), ws.data_ptr(), ws_bytes, st)
         nnz = int(row_ptrs[-1].item())
         vals = torch.empty(nnz, dtype=A.dtype, device=dev)
         cols = torch.empty(nnz, dtype=torch.int64, device=dev)
         if nnz > 0:
-            _lib.call("trnsparse_csr_from_dense_fill", m, n, A.data_ptr(), lda, code, thr, row_ptrs.data_ptr(),
-                      vals.data_ptr(), cols.data_ptr(), st)
+            # a gathered entry costs a 32-byte sector; a re-read costs the row's element bytes
+            if nnz * 64 < m * n * A.element_size():
+                _lib.call("trnsparse_csr_from_dense_fill_masked", m, n, A.data_ptr(), lda, code, row_ptrs.data_ptr(),
+                          mask.data_ptr(), vals.data_ptr(), cols.data_ptr(), st)
+            else:
+                _lib.call("trnsparse_csr_from_dense_fill", m, n, A.data_ptr(), lda, code, thr, row_ptrs.data_ptr(),
+                          vals.data_ptr(), cols.data_ptr(), st)
     return CSRMatrix(values=vals, col_indices=cols, row_ptrs=row_ptrs, shape=(m, n))
 
 
