@@ -231,7 +231,10 @@ TRNSPARSE_API int trnsparse_bsr_spmm_tc_plan(int64_t n_block_rows, const int* ro
 
 /* hi = tf32(src), lo = tf32(src - hi), elementwise over `count` floats
  * (round to nearest, ties away). Used once per BSR matrix for the F32
- * tensor-core path. */
+ * tensor-core path. hi NULL: only lo = tf32(src - src with its low 13 mantissa
+ * bits cleared), for passing src itself as blocks_hi (a kind::tf32 MMA reads
+ * only the top 10 mantissa bits of an fp32 operand); one extra copy of the
+ * blocks instead of two. */
 TRNSPARSE_API int trnsparse_bsr_split_tf32(int64_t count, const float* src, float* hi, float* lo, void* stream);
 
 /* C = (A o mask) @ B with the Schwarz screening mask applied inside the

@@ -305,7 +305,7 @@ inline int64_t bf16_pad_ld(int64_t k) { return std::max<int64_t>(64, round_up(k,
 using namespace tsb;
 
 extern "C" int trnsparse_bsr_split_tf32(int64_t count, const float* src, float* hi, float* lo, void* stream) {
-  TSB_REQUIRE(count >= 0 && (count == 0 || (src && hi && lo)), "bsr_split_tf32: bad argument");
+  TSB_REQUIRE(count >= 0 && (count == 0 || (src && lo)), "bsr_split_tf32: bad argument");
   if (count == 0) return TRNSPARSE_OK;
   int64_t g = (count + 255) / 256;
   if (g > 8 * sm_count()) g = 8 * sm_count();

@@ -56,9 +56,16 @@ __global__ void split_tf32_kernel(int64_t n, const float* __restrict__ src, floa
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float x = src[i];
-    const float h = tf32_rna(x);
-    hi[i] = h;
-    lo[i] = tf32_rna(x - h);
+    if (hi != nullptr) {
+      const float h = tf32_rna(x);
+      hi[i] = h;
+      lo[i] = tf32_rna(x - h);
+    } else {
+      // src itself is the hi operand: a kind::tf32 MMA reads an fp32 operand's sign,
+      // exponent and top 10 mantissa bits, so the part it drops is x minus x with its
+      // low 13 bits cleared (exact in fp32)
+      lo[i] = tf32_rna(x - __uint_as_float(__float_as_uint(x) & 0xffffe000u));
+    }
   }
 }
 

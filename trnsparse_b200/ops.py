@@ -341,17 +341,19 @@ def _tc_plan(A: BSRMatrix, lay: dict, dev: torch.device, k: int) -> tuple[torch.
 
 
 def _tf32_split(lay: dict, dev: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """The 3xTF32 operands of the fp32 blocks: the blocks themselves as the high part (the
+    tensor core reads their top 10 mantissa bits) and, cached with the layout, the
+    residual it drops as the low part: one extra copy of the blocks."""
     hit = lay.get("tf32_split")
     if hit is None:
         blocks = lay["blocks"]
         if blocks.dtype != torch.float32:
             blocks = blocks.float().contiguous()
-        hi = torch.empty_like(blocks)
         lo = torch.empty_like(blocks)
         with torch.cuda.device(dev):
-            _lib.call("trnsparse_bsr_split_tf32", blocks.numel(), blocks.data_ptr(), hi.data_ptr(), lo.data_ptr(),
+            _lib.call("trnsparse_bsr_split_tf32", blocks.numel(), blocks.data_ptr(), None, lo.data_ptr(),
                       _lib.stream_handle(dev))
-        hit = lay["tf32_split"] = (hi, lo)
+        hit = lay["tf32_split"] = (blocks, lo)
     return hit
 
 
