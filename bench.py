@@ -269,6 +269,7 @@ def run_ours(args, ws, rank, local):
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(ach / pk["hbm_gbs"], 4), "peak_source": pk["source"] + " (burst copy)",
+                     "frac_of_nominal_8tbs": round(ach / 8000.0, 4),
                      "traffic": NCU_TRAFFIC["csr_spmv_warp_kernel"],
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch on this "
                      "workload (L2 flushed before it)", "kernel": "csr_spmv_warp_kernel<int,float,2,384>"},
