@@ -1310,6 +1310,55 @@ int coo_bucketed_sort(int esz, int64_t m, int64_t n, int64_t nnz, int nb, int64_
                                     keys, cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
   }
 }
+
+// The bucketed COO -> CSR on a workspace laid out as trnsparse_coo_to_csr's (entries with
+// an out-of-range index are left out and flag `bad`): count, scan, partition, per-bucket
+// sort, then the warp / CTA sorts of the longer rows. values may be null (then the entry
+// index is emitted as an int64 per entry).
+int coo_to_csr_bucketed(int64_t m, int64_t n, int64_t nnz, const long long* rows, const long long* cols,
+                        const void* values, int esz, long long* row_ptr, long long* cols_out, void* values_out,
+                        void* ws, cudaStream_t st) {
+  unsigned long long* keys = static_cast<unsigned long long*>(ws);
+  unsigned long long* keys2 = keys + nnz;
+  unsigned long long* cursor = keys2 + nnz;  // m entries
+  long long* part = reinterpret_cast<long long*>(cursor + m + 1);
+  long long* mid_rows = reinterpret_cast<long long*>(reinterpret_cast<uint8_t*>(part) + scan_ws_bytes(m));
+  long long* long_rows = mid_rows + m;
+  unsigned long long* n_mid = reinterpret_cast<unsigned long long*>(long_rows + m);
+  unsigned long long* n_long = n_mid + 1;
+  int* bad = reinterpret_cast<int*>(n_long + 1);
+  cudaError_t e = cudaMemsetAsync(n_mid, 0, 24, st);  // n_mid, n_long and bad
+  if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
+  const int nb = static_cast<int>((m + kBucketRows - 1) / kBucketRows);
+  const int64_t chunk = coo_chunk(nnz, nb);
+  const int64_t G = nnz > 0 ? (nnz + chunk - 1) / chunk : 1;
+  uint8_t* pval = reinterpret_cast<uint8_t*>(n_mid) + 32;  // past n_mid, n_long, bad (8 bytes per entry)
+  uint16_t* plrow = reinterpret_cast<uint16_t*>(pval + 8 * (size_t)nnz);
+  long long* cm = reinterpret_cast<long long*>(
+      (reinterpret_cast<uintptr_t>(plrow + nnz) + 15) & ~static_cast<uintptr_t>(15));  // nb * G + 1 cells
+  long long* cpart = cm + nb * G + 1;                                                   // its scan partials
+  if (nnz > 0) {
+    coo_bucket_count_kernel<<<(unsigned)G, 256, 0, st>>>(nnz, m, n, nb, chunk, rows, cols, cm, bad);
+    TSB_CHECK_LAUNCH("coo_to_csr: bucket count");
+  } else {
+    e = cudaMemsetAsync(cm, 0, sizeof(long long) * (nb * G + 1), st);
+    if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear counts");
+  }
+  int rc = exclusive_scan(cm, nb * G, cpart, st);
+  if (rc) return rc;
+  rc = coo_bucketed_sort(esz, m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, keys2, pval, row_ptr, keys,
+                         cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+  if (rc || nnz == 0) return rc;
+  // the rows of more than kTiny entries (listed by the bucket pass)
+  const uint8_t* vin = static_cast<const uint8_t*>(values);
+  const int vesz = values ? esz : 8;
+  coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, vin, vesz, cols_out,
+                                                     (uint8_t*)values_out);
+  coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(row_ptr, long_rows, n_long, keys, keys2, vin, vesz,
+                                                               cols_out, (uint8_t*)values_out);
+  TSB_CHECK_LAUNCH("coo_to_csr: sort");
+  return TRNSPARSE_OK;
+}
 }  // namespace
 }  // namespace tsb
 
@@ -1349,40 +1398,15 @@ extern "C" int trnsparse_coo_to_csr(int64_t m, int64_t n, int64_t nnz, const lon
   unsigned long long* n_mid = reinterpret_cast<unsigned long long*>(long_rows + m);
   unsigned long long* n_long = n_mid + 1;
   int* bad = reinterpret_cast<int*>(n_long + 1);
-  cudaError_t e = cudaMemsetAsync(n_mid, 0, 24, st);  // n_mid, n_long and bad
-  if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
+  cudaError_t e = cudaSuccess;
   if (m > 0 && m <= static_cast<int64_t>(kBucketRows) * kMaxBuckets) {
     // bucketed path: no per-entry global atomic (see coo_bucket_*_kernel)
-    const int nb = static_cast<int>((m + kBucketRows - 1) / kBucketRows);
-    const int64_t chunk = coo_chunk(nnz, nb);
-    const int64_t G = nnz > 0 ? (nnz + chunk - 1) / chunk : 1;
-    uint8_t* pval = reinterpret_cast<uint8_t*>(n_mid) + 32;  // past n_mid, n_long, bad (8 bytes per entry)
-    uint16_t* plrow = reinterpret_cast<uint16_t*>(pval + 8 * (size_t)nnz);
-    long long* cm = reinterpret_cast<long long*>(
-        (reinterpret_cast<uintptr_t>(plrow + nnz) + 15) & ~static_cast<uintptr_t>(15));  // nb * G + 1 cells
-    long long* cpart = cm + nb * G + 1;                                                   // its scan partials
-    if (nnz > 0) {
-      coo_bucket_count_kernel<<<(unsigned)G, 256, 0, st>>>(nnz, m, n, nb, chunk, rows, cols, cm, bad);
-      TSB_CHECK_LAUNCH("coo_to_csr: bucket count");
-    } else {
-      e = cudaMemsetAsync(cm, 0, sizeof(long long) * (nb * G + 1), st);
-      if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear counts");
-    }
-    int rc = exclusive_scan(cm, nb * G, cpart, st);
-    if (rc) return rc;
-    rc = coo_bucketed_sort(esz, m, n, nnz, nb, chunk, G, rows, cols, values, cm, plrow, keys2, pval, row_ptr, keys,
-                           cols_out, values_out, mid_rows, n_mid, long_rows, n_long, st);
+    int rc = coo_to_csr_bucketed(m, n, nnz, rows, cols, values, esz, row_ptr, cols_out, values_out, ws, st);
     if (rc) return rc;
     if (nnz == 0) return TRNSPARSE_OK;
-    // the rows of more than kTiny entries (listed by the bucket pass)
-    coo_sort_mid_kernel<<<grid_for(m, 8), 256, 0, st>>>(row_ptr, mid_rows, n_mid, keys, (const uint8_t*)values,
-                                                       esz, cols_out, (uint8_t*)values_out);
-    coo_sort_long_kernel<<<grid_for(m, 1), kSortThreads, 0, st>>>(row_ptr, long_rows, n_long, keys, keys2,
-                                                                 (const uint8_t*)values, esz, cols_out,
-                                                                 (uint8_t*)values_out);
-    TSB_CHECK_LAUNCH("coo_to_csr: sort");
   } else {
-    e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
+    e = cudaMemsetAsync(n_mid, 0, 24, st);  // n_mid, n_long and bad
+    if (e == cudaSuccess) e = cudaMemsetAsync(row_ptr, 0, sizeof(long long) * (m + 1), st);
     if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: clear");
     if (nnz > 0) {
       coo_count_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, m, n, rows, cols,
@@ -1452,6 +1476,14 @@ extern "C" int trnsparse_csr_transpose(int64_t m, int64_t n, int64_t nnz, int in
     else
       csr_entry_coords_kernel<long long><<<grid_for(m, 8), 256, 0, st>>>(
           m, static_cast<const long long*>(row_ptr), static_cast<const long long*>(col_idx), strict, trow, tcol);
+    TSB_CHECK_LAUNCH("csr_transpose: coordinates");
+  }
+  if (n > 0 && n <= static_cast<int64_t>(kBucketRows) * kMaxBuckets) {
+    // the entries as a COO of A^T (diagonal entries left out of the strict triangle carry
+    // row -1, which the bucketed sort skips); the emitted "values" are the entry indices
+    return coo_to_csr_bucketed(n, m, m > 0 ? nnz : 0, trow, tcol, nullptr, 0, row_ptr_t, col_t, perm, cws, st);
+  }
+  if (nnz > 0 && m > 0) {
     coo_count_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, n, m, trow, tcol,
                                                         reinterpret_cast<unsigned long long*>(row_ptr_t), bad, 1);
     TSB_CHECK_LAUNCH("csr_transpose: count");
