@@ -68,9 +68,13 @@ TRNSPARSE_API int trnsparse_csr_spmv(int64_t m, int64_t n, int64_t nnz, int inde
  * rows keep the vector path) runs once the first x_need[i] entries of x (the
  * chunk's largest column + 1, non-decreasing) have arrived, and its rows are
  * copied back on a second copy stream while later chunks compute. x_dev (n)
- * and out_dev (m) are device scratch. `stream` waits for the last copy: after
- * synchronising it, out_host is complete. row_splits / x_need: host arrays,
- * n_chunks <= 64. Calls on one device are issued one at a time (a lock). */
+ * is device scratch; out_dev (m) is device scratch, or out_host itself, in
+ * which case the chunks' kernels write y straight into the pinned host buffer
+ * and no copy back is issued (measured faster: the device-to-host copies
+ * otherwise compete with the x uploads). `stream` waits for the last copy:
+ * after synchronising it, out_host is complete. row_splits / x_need: host
+ * arrays, n_chunks <= 64. Calls on one device are issued one at a time (a
+ * lock). */
 TRNSPARSE_API int trnsparse_csr_spmv_host(int64_t m, int64_t n, int64_t nnz, int index_type, int dtype,
                             const void* row_ptrs, const void* col_indices, const void* values,
                             const void* x_host, double alpha, void* out_host, void* x_dev, void* out_dev,

@@ -752,7 +752,8 @@ int pipe_ctx(PipeCtx** out) {
 
 // y = alpha A x with x and y in pinned host memory: x goes up in prefix pieces on one copy
 // stream, row chunk i runs once the first x_need[i] entries of x have arrived, and its rows
-// go back on a second copy stream while later chunks compute; the caller's stream waits
+// go back on a second copy stream while later chunks compute (or, with out_dev == out_host,
+// the kernels store them into the pinned host buffer themselves); the caller's stream waits
 // for the last copy, so synchronising it (or any later work on it) sees y complete.
 extern "C" int trnsparse_csr_spmv_host(int64_t m, int64_t n, int64_t nnz, int index_type, int dtype,
                                        const void* row_ptrs, const void* col_indices, const void* values,
@@ -816,11 +817,13 @@ extern "C" int trnsparse_csr_spmv_host(int64_t m, int64_t n, int64_t nnz, int in
                  : launch_spmv<int64_t, double>(b - a, nnz, rp, col_indices, values, x_dev, alpha, nullptr, 0.0, o,
                                                 st);
       if (rc) return rc;
-      e = cudaEventRecord(c->done[i], st);
-      if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->done[i], 0);
-      if (e == cudaSuccess)
-        e = cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + a * es, o, (b - a) * es, cudaMemcpyDeviceToHost,
-                            c->s_out);
+      if (out_dev != out_host) {  // otherwise the kernel has written the rows to host memory itself
+        e = cudaEventRecord(c->done[i], st);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->done[i], 0);
+        if (e == cudaSuccess)
+          e = cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + a * es, o, (b - a) * es, cudaMemcpyDeviceToHost,
+                              c->s_out);
+      }
     }
   }
   if (e == cudaSuccess) e = cudaEventRecord(c->end, c->s_out);

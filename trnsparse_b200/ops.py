@@ -108,12 +108,13 @@ def _spmv_pipelined(A: CSRMatrix, lay: dict, x: torch.Tensor, alpha: float, dev:
         lay[key] = plan
     nch, splits, need = plan
     xd = torch.empty(n, dtype=A.dtype, device=dev)
-    out = torch.empty(m, dtype=A.dtype, device=dev)
     host = torch.empty(m, dtype=A.dtype, pin_memory=True)
     st = torch.cuda.current_stream(dev)
+    # the row chunks' kernels write y straight into the pinned host buffer (out_dev == out_host):
+    # no device-to-host copies competing with the x uploads for the copy engines
     _lib.call("trnsparse_csr_spmv_host", m, n, A.nnz, _lib.index_code(lay["row_ptrs"].dtype), _lib.dtype_code(A.dtype),
               _lib.ptr(lay["row_ptrs"]), _lib.ptr(lay["col_indices"]), _lib.ptr(lay["values"]), x.data_ptr(),
-              float(alpha), host.data_ptr(), xd.data_ptr(), out.data_ptr(), nch, splits.data_ptr(), need.data_ptr(),
+              float(alpha), host.data_ptr(), xd.data_ptr(), host.data_ptr(), nch, splits.data_ptr(), need.data_ptr(),
               st.cuda_stream)
     st.synchronize()
     return host
