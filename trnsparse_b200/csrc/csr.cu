@@ -448,7 +448,7 @@ csr_spmv_warp_kernel(int64_t m, int64_t nnz, const I* __restrict__ rp, const I* 
 // is memory-latency bound and occupancy is what keeps enough B-row loads in
 // flight (config 2b: 0.39 ms at four CTAs per SM, 0.30 ms at eight); the wider
 // instantiations would spill at 32 registers and keep four.
-template <typename I, typename T, int VEC>
+template <typename I, typename T, int VEC, bool SMALL = false>
 __global__ void __launch_bounds__(kThreads, (sizeof(I) == 4 && sizeof(T) == 4 && VEC > 1) ? 8 : 4)
 csr_spmm_kernel(int64_t m, int64_t k, int64_t nnz, const I* __restrict__ rp, const I* __restrict__ ci,
                 const T* __restrict__ v, const T* __restrict__ B, int64_t ldb, T alpha,
@@ -494,7 +494,9 @@ csr_spmm_kernel(int64_t m, int64_t k, int64_t nnz, const I* __restrict__ rp, con
           const I* cc = cs + st.dc;
 #pragma unroll 4
           for (int j = static_cast<int>(a); j < static_cast<int>(b); ++j) {
-            const VT bv = __ldg(bc + static_cast<int64_t>(cc[j]) * ldv);
+            // SMALL: B fits 2^31 vector units, so 32-bit row offsets (one multiply per row)
+            const VT bv = SMALL ? __ldg(bc + static_cast<int>(cc[j]) * static_cast<int>(ldv))
+                                : __ldg(bc + static_cast<int64_t>(cc[j]) * ldv);
             const T val = vv[j];
             const T* bp = reinterpret_cast<const T*>(&bv);
 #pragma unroll
@@ -602,7 +604,7 @@ int launch_spmv(int64_t m, int64_t nnz, const void* rp, const void* ci, const vo
 }
 
 template <typename I, typename T>
-int launch_spmm(int64_t m, int64_t k, int64_t nnz, const void* rp, const void* ci, const void* v,
+int launch_spmm(int64_t m, int64_t n, int64_t k, int64_t nnz, const void* rp, const void* ci, const void* v,
                 const void* B, int64_t ldb, double alpha, const void* C, int64_t ldc, double beta,
                 void* out, int64_t ldo, cudaStream_t st) {
   constexpr int V = Vec16<T>::n;
@@ -621,8 +623,10 @@ int launch_spmm(int64_t m, int64_t k, int64_t nnz, const void* rp, const void* c
   const size_t sm = smem_bytes<I, T>(rows, cap);
   const int64_t grid = (m + rows - 1) / rows;
   if (grid > 0x7fffffff) return fail(TRNSPARSE_ERR_ARG, "csr_spmm: m=%lld too large", (long long)m);
+  // every gathered B row offset (in vector units) fits 31 bits
+  const bool small_idx = vec_cols && n * (ldb / V) + nchunk < (1ll << 31);
   if (vec_cols) {
-    auto kern = csr_spmm_kernel<I, T, V>;
+    auto kern = small_idx ? csr_spmm_kernel<I, T, V, true> : csr_spmm_kernel<I, T, V, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return cuda_status(e, "csr_spmm: set smem");
     kern<<<(unsigned)grid, kThreads, sm, st>>>(m, k, nnz, (const I*)rp, (const I*)ci, (const T*)v,
@@ -845,11 +849,11 @@ extern "C" int trnsparse_csr_spmm(int64_t m, int64_t n, int64_t k, int64_t nnz, 
   TSB_REQUIRE(C == nullptr || ldc >= k, "csr_spmm: ldc smaller than k");
   cudaStream_t st = as_stream(stream);
   if (dtype == TRNSPARSE_F32) {
-    if (index_type == TRNSPARSE_I32) return launch_spmm<int32_t, float>(m, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
-    if (index_type == TRNSPARSE_I64) return launch_spmm<int64_t, float>(m, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
+    if (index_type == TRNSPARSE_I32) return launch_spmm<int32_t, float>(m, n, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
+    if (index_type == TRNSPARSE_I64) return launch_spmm<int64_t, float>(m, n, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
   } else if (dtype == TRNSPARSE_F64) {
-    if (index_type == TRNSPARSE_I32) return launch_spmm<int32_t, double>(m, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
-    if (index_type == TRNSPARSE_I64) return launch_spmm<int64_t, double>(m, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
+    if (index_type == TRNSPARSE_I32) return launch_spmm<int32_t, double>(m, n, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
+    if (index_type == TRNSPARSE_I64) return launch_spmm<int64_t, double>(m, n, k, nnz, row_ptrs, col_indices, values, B, ldb, alpha, C, ldc, beta, out, ldo, st);
   } else {
     return fail(TRNSPARSE_ERR_DTYPE, "csr_spmm: dtype %d not supported (F32, F64)", dtype);
   }
