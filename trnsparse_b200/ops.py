@@ -74,6 +74,7 @@ def spmv(
 
 
 _SPMV_PIPE_CHUNKS = 4          # row / x chunks of the host-buffer pipeline (4 measured best of 4-32)
+_SPMV_DIRECT_Y = os.environ.get("TRNSPARSE_SPMV_DIRECT_Y", "1") != "0"
 _SPMV_PIPE_MIN_ROWS = 1 << 18  # smaller products are not worth splitting
 
 
@@ -110,11 +111,12 @@ def _spmv_pipelined(A: CSRMatrix, lay: dict, x: torch.Tensor, alpha: float, dev:
     xd = torch.empty(n, dtype=A.dtype, device=dev)
     host = torch.empty(m, dtype=A.dtype, pin_memory=True)
     st = torch.cuda.current_stream(dev)
-    # the row chunks' kernels write y straight into the pinned host buffer (out_dev == out_host):
-    # no device-to-host copies competing with the x uploads for the copy engines
+    # _SPMV_DIRECT_Y: the row chunks' kernels write y straight into the pinned host buffer
+    # (out_dev == out_host); otherwise y goes through a device buffer and copies back
+    out = host if _SPMV_DIRECT_Y else torch.empty(m, dtype=A.dtype, device=dev)
     _lib.call("trnsparse_csr_spmv_host", m, n, A.nnz, _lib.index_code(lay["row_ptrs"].dtype), _lib.dtype_code(A.dtype),
               _lib.ptr(lay["row_ptrs"]), _lib.ptr(lay["col_indices"]), _lib.ptr(lay["values"]), x.data_ptr(),
-              float(alpha), host.data_ptr(), xd.data_ptr(), host.data_ptr(), nch, splits.data_ptr(), need.data_ptr(),
+              float(alpha), host.data_ptr(), xd.data_ptr(), out.data_ptr(), nch, splits.data_ptr(), need.data_ptr(),
               st.cuda_stream)
     st.synchronize()
     return host
