@@ -1278,6 +1278,10 @@ int coo_bucketed_launch(int64_t m, int64_t n, int64_t nnz, int nb, int64_t chunk
   auto bk = coo_bucket_sort_kernel<ESZ>;
   const size_t budget = TSB_COO_BUCKET_KB * 1024;
   const int cap = static_cast<int>((budget - coo_bucket_smem_fixed()) / coo_bucket_entry_bytes(ESZ)) & ~7;
+  // a bucket's short rows hold at most kBucketRows * kTiny entries: that many sub-ranges of
+  // cap - kTiny must fit the kernel's boundary table
+  TSB_REQUIRE(cap > 2 * kTiny && (kBucketRows * kTiny + cap - kTiny - 1) / (cap - kTiny) <= kMaxSub,
+              "coo_to_csr: bucket staging area too small (%d entries)", cap);
   const size_t bsm = coo_bucket_smem_fixed() + static_cast<size_t>(cap) * coo_bucket_entry_bytes(ESZ) + 16;
   cudaError_t e = cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
   if (e != cudaSuccess) return cuda_status(e, "coo_to_csr: bucket smem");
