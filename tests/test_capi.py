@@ -197,3 +197,12 @@ def test_new_entry_points_validate_before_cuda():
     assert lib.trnsparse_bsr_attention_backward_tc(1, 128, 96, p, p, p, p, 0, 0, 0, 0, p, p, p, p, p, None, p, p,
                                                    p, 1.0, p, 1 << 30, None) == _lib.ERR_ARG
     assert _lib.raw("trnsparse_bsr_attention_backward_tc_workspace_size")(2, 256, 128, 3) == 4 * (2 * 512 + 3 * 2 * 2 * 128 * 128)
+
+
+def test_csr_from_dense_mask_bytes():
+    """Size of the kept-entry bit mask of CSR from_dense (host function, no GPU): one
+    uint32 word per 32 columns of every row, zero for negative sizes."""
+    f = _lib.raw("trnsparse_csr_from_dense_mask_bytes")
+    for m, n in [(0, 0), (1, 1), (3, 31), (3, 32), (3, 33), (8192, 8192), (7, 100000)]:
+        assert f(m, n) == 4 * m * ((n + 31) // 32)
+    assert f(-1, 5) == 0 and f(5, -1) == 0
