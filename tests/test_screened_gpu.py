@@ -36,7 +36,9 @@ def _fock(n, k, seed, sort=False):
     return A, Q, B
 
 
-@pytest.mark.parametrize("n,k,sort", [(512, 96, False), (640, 256, True), (300, 40, True)])
+@pytest.mark.parametrize("n,k,sort", [(512, 96, False), (640, 256, True), (300, 40, True),
+                                      # N in (256, 512]: both 256-wide N tiles in one work unit
+                                      (896, 512, False), (300, 300, True)])
 def test_screened_pair_bounds(n, k, sort):
     A, Q, B = _fock(n, k, seed=n, sort=sort)
     ref = oracle.screened_spmm_pair(A, Q, B, 1e-10)
@@ -55,12 +57,13 @@ def test_screened_vector_form_and_host_tensors():
     assert got.device.type == "cpu" and rel_fro(got, ref) <= 1e-5
 
 
-def test_screened_block_skip_exact_zero_rows():
+@pytest.mark.parametrize("k", [32, 400])
+def test_screened_block_skip_exact_zero_rows(k):
     n = 512
     A = torch.randn(n, n)
     d = torch.ones(n)
     d[:256] = 1e-12  # rows/cols 0..255 screened against everything
-    B = torch.randn(n, 32)
+    B = torch.randn(n, k)
     got = ts.screened_spmm(A.cuda(), d.cuda(), B.cuda(), 1e-6).cpu()
     assert torch.count_nonzero(got[:256]) == 0
     assert rel_fro(got, oracle.screened_spmm(A, d, B, 1e-6)) <= 1e-5
