@@ -14,8 +14,10 @@
 // 128-byte-swizzled layout; the 1-D form un-swizzles offsets to find each
 // element's row and column); warp 1 issues the 3xTF32 tcgen05.mma. A chunk
 // with no surviving pair issues no MMA (the block skip). Work units are
-// (128-row tile, contiguous range of 128-wide K blocks); units that split a
-// row tile combine through float reductions into a zeroed C.
+// (128-row tile, N tile, contiguous range of 128-wide K blocks); units that
+// split a row tile combine through float reductions into a zeroed C. When N
+// spans exactly two 256-wide tiles, screened_tc2_kernel takes both N tiles in
+// one unit so each masked A chunk is loaded and transformed once.
 #include <cstdlib>
 
 #include "tc_common.cuh"
