@@ -42,7 +42,7 @@ def test_tc_single_block_known_product():
     assert ts._lib.device_error() == 0
 
 
-@pytest.mark.parametrize("k", [8, 16, 40, 64, 100, 128, 200, 256, 384])
+@pytest.mark.parametrize("k", [8, 16, 40, 64, 100, 128, 200, 256, 384, 512, 700])
 def test_tc_fp32_widths(k):
     A = _random_bsr(3, 4, 0.6, seed=k)
     B = torch.randn(A.shape[1], k, generator=torch.Generator().manual_seed(100 + k))
@@ -82,7 +82,7 @@ def test_tc_config1():
     assert rel_fro(got, got2) <= 1e-6
 
 
-@pytest.mark.parametrize("k", [64, 256])
+@pytest.mark.parametrize("k", [64, 256, 300, 512])
 def test_tc_bf16(k):
     A = _random_bsr(4, 4, 0.5, seed=11, dtype=torch.bfloat16)
     B = torch.randn(A.shape[1], k, generator=torch.Generator().manual_seed(12)).to(torch.bfloat16)
