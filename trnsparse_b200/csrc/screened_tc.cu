@@ -79,6 +79,42 @@ __device__ __forceinline__ ScWalk sc_walk(int64_t W, int nkb, int nt) {
   return ScWalk{W * blockIdx.x / G, W * (blockIdx.x + 1) / G, nkb, nt};
 }
 
+// One row of a 128 x 32 chunk, in place: A o mask split into tf32 hi (over A) and lo (over
+// Q, which mode 2 reads its bounds from first). The row's 8 16-byte chunks are 128-byte
+// swizzled; they are visited rotated so 8 neighbouring rows hit 8 different banks. Returns
+// whether any pair of the row survives.
+__device__ __forceinline__ int sc_mask_split_row(float4* arow, float4* lrow, int tr, int mode, float qi, int kx,
+                                                 int64_t K, const float* __restrict__ q_vec, float t) {
+  int keep = 0;
+#pragma unroll
+  for (int pp = 0; pp < 8; ++pp) {
+    const int p = (pp + tr) & 7;
+    const int L = p ^ (tr & 7);  // logical 16-byte chunk held by physical chunk p
+    const float4 a = arow[p];
+    float4 qv;
+    if (mode == 2) {
+      qv = lrow[p];
+    } else {
+      const int64_t c0 = kx + 4 * L;
+      float qc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) qc[u] = (c0 + u < K) ? __fsqrt_rn(fabsf(__ldg(q_vec + c0 + u))) : 0.f;
+      qv = make_float4(__fmul_rn(qi, qc[0]), __fmul_rn(qi, qc[1]), __fmul_rn(qi, qc[2]), __fmul_rn(qi, qc[3]));
+    }
+    const float v[4] = {qv.x > t ? a.x : 0.f, qv.y > t ? a.y : 0.f, qv.z > t ? a.z : 0.f, qv.w > t ? a.w : 0.f};
+    keep |= (qv.x > t) | (qv.y > t) | (qv.z > t) | (qv.w > t);
+    float h[4], l[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      h[u] = tf32_rna(v[u]);
+      l[u] = tf32_rna(v[u] - h[u]);
+    }
+    arow[p] = make_float4(h[0], h[1], h[2], h[3]);
+    lrow[p] = make_float4(l[0], l[1], l[2], l[3]);
+  }
+  return keep;
+}
+
 // mode 1: q_vec (length K == M) holds diag integrals, mask = fl(Qi*Qj) > t
 // mode 2: tq maps the 2-D bound matrix Q (M x K), mask = Q > t
 // Persistent: gridDim.x CTAs split the (output tile, K block) space evenly (sc_walk).
@@ -216,36 +252,9 @@ screened_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant
       for (int kc = g.kb0 * 4; kc < g.kb1 * 4; ++kc, ++it) {
         const int s = it % S, use = it / S;
         if (*abort_flag || !mbar_wait(&Bs.full[s], use & 1)) { ok = false; break; }
-        const int kx = kc * 32;
-        float4* arow = reinterpret_cast<float4*>(a_hi(s) + tr * 128);
-        float4* lrow = reinterpret_cast<float4*>(a_lo(s) + tr * 128);
-        int keep = 0;
-#pragma unroll
-        for (int pp = 0; pp < 8; ++pp) {
-          const int p = (pp + tr) & 7;   // rotate so 8 neighbouring rows hit 8 different banks
-          const int L = p ^ (tr & 7);    // logical 16-byte chunk held by physical chunk p
-          float4 a = arow[p];
-          float4 qv;
-          if (mode == 2) {
-            qv = lrow[p];
-          } else {
-            const int64_t c0 = kx + 4 * L;
-            float qc[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) qc[u] = (c0 + u < K) ? __fsqrt_rn(fabsf(__ldg(q_vec + c0 + u))) : 0.f;
-            qv = make_float4(__fmul_rn(qi, qc[0]), __fmul_rn(qi, qc[1]), __fmul_rn(qi, qc[2]), __fmul_rn(qi, qc[3]));
-          }
-          float v[4] = {qv.x > t ? a.x : 0.f, qv.y > t ? a.y : 0.f, qv.z > t ? a.z : 0.f, qv.w > t ? a.w : 0.f};
-          keep |= (qv.x > t) | (qv.y > t) | (qv.z > t) | (qv.w > t);
-          float h[4], l[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            h[u] = tf32_rna(v[u]);
-            l[u] = tf32_rna(v[u] - h[u]);
-          }
-          arow[p] = make_float4(h[0], h[1], h[2], h[3]);
-          lrow[p] = make_float4(l[0], l[1], l[2], l[3]);
-        }
+        const int keep = sc_mask_split_row(reinterpret_cast<float4*>(a_hi(s) + tr * 128),
+                                           reinterpret_cast<float4*>(a_lo(s) + tr * 128), tr, mode, qi, kc * 32, K,
+                                           q_vec, t);
         const int wkeep = __any_sync(0xffffffffu, keep);
         if (lane == 0) Bs.survive[s][w4] = wkeep;
         fence_proxy_async_smem();  // generic-proxy writes -> tcgen05 (async proxy) reads
@@ -493,36 +502,9 @@ screened_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constan
       for (int kc = g.kb0 * 4; kc < g.kb1 * 4; ++kc, ++ia) {
         const int sa = ia & 1, ua = ia >> 1;
         if (*abort_flag || !mbar_wait(&Bs.a_full[sa], ua & 1)) { ok = false; break; }
-        const int kx = kc * 32;
-        float4* arow = reinterpret_cast<float4*>(a_hi(sa) + tr * 128);
-        float4* lrow = reinterpret_cast<float4*>(a_lo(sa) + tr * 128);
-        int keep = 0;
-#pragma unroll
-        for (int pp = 0; pp < 8; ++pp) {
-          const int p = (pp + tr) & 7;   // rotate so 8 neighbouring rows hit 8 different banks
-          const int L = p ^ (tr & 7);    // logical 16-byte chunk held by physical chunk p
-          float4 a = arow[p];
-          float4 qv;
-          if (mode == 2) {
-            qv = lrow[p];
-          } else {
-            const int64_t c0 = kx + 4 * L;
-            float qc[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) qc[u] = (c0 + u < K) ? __fsqrt_rn(fabsf(__ldg(q_vec + c0 + u))) : 0.f;
-            qv = make_float4(__fmul_rn(qi, qc[0]), __fmul_rn(qi, qc[1]), __fmul_rn(qi, qc[2]), __fmul_rn(qi, qc[3]));
-          }
-          float v[4] = {qv.x > t ? a.x : 0.f, qv.y > t ? a.y : 0.f, qv.z > t ? a.z : 0.f, qv.w > t ? a.w : 0.f};
-          keep |= (qv.x > t) | (qv.y > t) | (qv.z > t) | (qv.w > t);
-          float hh[4], l[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            hh[u] = tf32_rna(v[u]);
-            l[u] = tf32_rna(v[u] - hh[u]);
-          }
-          arow[p] = make_float4(hh[0], hh[1], hh[2], hh[3]);
-          lrow[p] = make_float4(l[0], l[1], l[2], l[3]);
-        }
+        const int keep = sc_mask_split_row(reinterpret_cast<float4*>(a_hi(sa) + tr * 128),
+                                           reinterpret_cast<float4*>(a_lo(sa) + tr * 128), tr, mode, qi, kc * 32, K,
+                                           q_vec, t);
         const int wkeep = __any_sync(0xffffffffu, keep);
         if (lane == 0) Bs.survive[sa][w4] = wkeep;
         fence_proxy_async_smem();  // generic-proxy writes -> tcgen05 (async proxy) reads
